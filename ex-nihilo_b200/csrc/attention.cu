@@ -1,0 +1,319 @@
+// attention.cu -- the DiT's masked attention on the 5th-generation tensor
+// cores, head dim 128.
+//
+// Semantics of src/cuda/dit.cu:60-66 (xa_lim) and :208-336 (x_attend_mma):
+// query row g of the sequence sees keys 0 .. lim(g), with lim(g) = L-1 for
+// image rows (g >= p), b1-1 for a reference picture's rows (b0 <= g < b1)
+// and g otherwise (the prompt is causal); softmax(q k^T / sqrt(128)) v.
+// Queries of one pass are sequence rows q0 .. q0+nq-1 (q0 = the cached
+// prefix length on steps 2-8), keys rows 0 .. L-1 of the layer's K/V, whose
+// prefix rows persist from the first step (no copy, unlike
+// src/cuda-dit.lisp:207-218).
+//
+// One CTA = one (sample, head) and two tiles of 128 queries (a, b) that
+// share every K/V tile:
+//   warp 0      TMA: Q_a, Q_b once; K_j, V_j (128 keys x 128 dims, bf16)
+//   warp 1      tcgen05.mma: S_x = Q_x K_j^T into TMEM, O_x += P_x V_j
+//   warps 2..5  softmax of tile a, warps 6..9 of tile b: one query row per
+//               thread straight from TMEM (32x32b loads), P_x (bf16) into
+//               swizzled shared memory, O_x rescaled in TMEM only when the
+//               row maximum grows by more than 2^8
+// The MMA order PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) lets one tile's softmax
+// run while the tensor core serves the other.
+#include "exn_device.cuh"
+#include "exn_internal.h"
+
+namespace exn {
+
+int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                   const uint32_t* box);
+
+namespace {
+
+constexpr int ATT_THREADS = 320;
+constexpr int TILE = 128;                 // queries per tile, keys per K/V tile
+constexpr int HALF = TILE * 128;          // bytes of one 64-column swizzled half of a 128 x 128 bf16 tile
+constexpr int TILE_BYTES = 2 * HALF;      // 32 KB
+constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_K = 2 * TILE_BYTES, OFF_V = 3 * TILE_BYTES;
+constexpr int OFF_PA = 4 * TILE_BYTES, OFF_PB = 5 * TILE_BYTES, OFF_BAR = 6 * TILE_BYTES;
+constexpr int ATT_SMEM = OFF_BAR + 256 + 1024;
+constexpr uint32_t IDESC_S = idesc_bf16(128, 128);
+constexpr uint32_t IDESC_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (dims contiguous)
+constexpr float RESCALE_THRESHOLD = 8.0f;                          // log2 units
+
+__device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
+  return g >= p ? l - 1 : (g >= b0 && g < b1 ? b1 - 1 : g);
+}
+
+struct Bars {
+  uint64_t q_full, k_full, k_empty, v_full, v_empty;
+  uint64_t s_full[2], p_full[2], o_full[2];
+  uint64_t done;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
+                int b0, int b1, int width, float scale_log2, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, head = blockIdx.y, sample = blockIdx.z;
+  const int qlast = min(nq, (qt + 1) * 2 * TILE) - 1;
+  const int last_key = xa_lim(q0 + qlast, p, l, b0, b1);
+  const int nkv = last_key / TILE + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->k_full, 1);
+    mbar_init(&bars->k_empty, 1);
+    mbar_init(&bars->v_full, 1);
+    mbar_init(&bars->v_empty, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->p_full[x], 4);
+      mbar_init(&bars->o_full[x], 1);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+  // TMEM columns: S_a [0,128), S_b [128,256), O_a [256,384), O_b [384,512)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch(&tmQ);
+      tma_prefetch(&tmK);
+      tma_prefetch(&tmV);
+      const int hx = head * 128;
+      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
+      for (int x = 0; x < 2; ++x)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem + (x ? OFF_QB : OFF_QA) + hf * HALF, &tmQ, &bars->q_full, hx + hf * 64,
+                      qt * 2 * TILE + x * TILE, sample);
+      int k_issued = -1, v_issued = -1;
+      for (int j = 0; j < nkv; ++j) {
+        const uint32_t par = (j & 1) ^ 1;
+        if (!mbar_wait(&bars->k_empty, par, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&bars->k_full, TILE_BYTES);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem + OFF_K + hf * HALF, &tmK, &bars->k_full, hx + hf * 64, j * TILE, sample);
+        k_issued = j;
+        if (!mbar_wait(&bars->v_empty, par, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&bars->v_full, TILE_BYTES);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d(smem + OFF_V + hf * HALF, &tmV, &bars->v_full, hx + hf * 64, j * TILE, sample);
+        v_issued = j;
+      }
+      if (*abort_flag) {  // the copies in flight land before the CTA leaves
+        volatile int no_abort = 0;
+        mbar_wait(&bars->q_full, 0, &no_abort, nullptr, 0);
+        if (k_issued >= 0) mbar_wait(&bars->k_full, k_issued & 1, &no_abort, nullptr, 0);
+        if (v_issued >= 0) mbar_wait(&bars->v_full, v_issued & 1, &no_abort, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t qa = smem_u32(smem + OFF_QA), qb = smem_u32(smem + OFF_QB);
+      const uint32_t kk_base = smem_u32(smem + OFF_K), v_base = smem_u32(smem + OFF_V);
+      const uint32_t pa = smem_u32(smem + OFF_PA), pb = smem_u32(smem + OFF_PB);
+      auto issue_s = [&](uint32_t q_addr, uint32_t d) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t o = (kk >> 2) * HALF + (kk & 3) * 32;
+          umma_ss(d, sdesc_sw128(q_addr + o, 16, 1024), sdesc_sw128(kk_base + o, 16, 1024), IDESC_S,
+                  kk ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](uint32_t p_addr, uint32_t d, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(v_base + kk * 2048, HALF, 1024);
+          umma_ss(d, ad, bd, IDESC_PV, (acc || kk) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) &&
+                mbar_wait(&bars->k_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN);
+      if (ok) {
+        tc_fence_after();
+        issue_s(qa, tmem + 0);
+        umma_commit(&bars->s_full[0]);
+        issue_s(qb, tmem + 128);
+        umma_commit(&bars->s_full[1]);
+        umma_commit(&bars->k_empty);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const uint32_t par = j & 1;
+        const bool more = j + 1 < nkv;
+        if (!(ok = mbar_wait(&bars->v_full, par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+        if (!(ok = mbar_wait(&bars->p_full[0], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+        tc_fence_after();
+        issue_pv(pa, tmem + 256, j > 0);
+        if (!more) umma_commit(&bars->o_full[0]);
+        if (more) {
+          if (!(ok = mbar_wait(&bars->k_full, par ^ 1, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+          tc_fence_after();
+          issue_s(qa, tmem + 0);
+          umma_commit(&bars->s_full[0]);
+        }
+        if (!(ok = mbar_wait(&bars->p_full[1], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+        tc_fence_after();
+        issue_pv(pb, tmem + 384, j > 0);
+        umma_commit(&bars->v_empty);
+        if (!more) umma_commit(&bars->o_full[1]);
+        if (more) {
+          issue_s(qb, tmem + 128);
+          umma_commit(&bars->s_full[1]);
+          umma_commit(&bars->k_empty);
+        }
+      }
+      umma_commit(&bars->done);
+      volatile int no_abort = 0;
+      mbar_wait(&bars->done, 0, &no_abort, nullptr, 0);
+    }
+  } else {
+    // ---- softmax: tile x, TMEM lane quarter wq, query row r of the tile
+    const int x = (warp - 2) >> 2;
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const int qi = qt * 2 * TILE + x * TILE + r;  // query index within the pass
+    const int lim = xa_lim(q0 + qi, p, l, b0, b1);
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + x * 128;
+    const uint32_t o_addr = tmem + lane_off + 256 + x * 128;
+    uint8_t* prow = smem + (x ? OFF_PB : OFF_PA) + r * 128;
+    float m = -INFINITY, lsum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_warp(&bars->s_full[x], j & 1, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(s_addr + c * 32, rr);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(rr[i]);
+      }
+      const int key0 = j * TILE;
+      if (key0 + TILE - 1 > lim) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (key0 + c > lim) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      const float m_new = fmaxf(m, mx * scale_log2);
+      const bool need = m_new > m + RESCALE_THRESHOLD;
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2(m - m_new);
+        lsum *= alpha;
+        m = m_new;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(o_addr + c * 32, rr);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+          tmem_st32(o_addr + c * 32, rr);
+        }
+        tmem_st_wait();
+      }
+      float ps = 0.f;
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = fast_exp2(fmaf(s[c16 * 8 + i], scale_log2, -m));
+          ps += e[i];
+        }
+        const int half = c16 >> 3, cw = c16 & 7;
+        *reinterpret_cast<uint4*>(prow + half * HALF + ((cw ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
+                       pack_bf16x2(e[6], e[7]));
+      }
+      lsum += ps;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[x]);
+    }
+    if (ok && mbar_wait_warp(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
+      tc_fence_after();
+      const float inv = 1.f / lsum;
+      bf16* dst = out + (static_cast<long long>(sample) * nq + qi) * width + head * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(o_addr + c * 32, rr);
+        if (qi < nq) {
+          uint4* o = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = make_uint4(pack_bf16x2(__uint_as_float(rr[8 * i]) * inv, __uint_as_float(rr[8 * i + 1]) * inv),
+                              pack_bf16x2(__uint_as_float(rr[8 * i + 2]) * inv, __uint_as_float(rr[8 * i + 3]) * inv),
+                              pack_bf16x2(__uint_as_float(rr[8 * i + 4]) * inv, __uint_as_float(rr[8 * i + 5]) * inv),
+                              pack_bf16x2(__uint_as_float(rr[8 * i + 6]) * inv, __uint_as_float(rr[8 * i + 7]) * inv));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
+  if (a.nq <= 0 || a.l <= 0 || a.width % 128 || a.heads * 128 != a.width || a.kv_rows < a.l) return -1;
+  if (a.q0 + a.nq > a.l) return -1;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64, TILE, 1};
+  const uint64_t dq[3] = {static_cast<uint64_t>(a.width), static_cast<uint64_t>(a.nq),
+                          static_cast<uint64_t>(a.batch)};
+  const uint64_t sq[2] = {static_cast<uint64_t>(a.width) * 2, static_cast<uint64_t>(a.nq) * a.width * 2};
+  const uint64_t dk[3] = {static_cast<uint64_t>(a.width), static_cast<uint64_t>(a.l), static_cast<uint64_t>(a.batch)};
+  const uint64_t sk[2] = {static_cast<uint64_t>(a.width) * 2, static_cast<uint64_t>(a.kv_rows) * a.width * 2};
+  if (make_tmap_bf16(&tq, a.q, 3, dq, sq, box) || make_tmap_bf16(&tk, a.k, 3, dk, sk, box) ||
+      make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
+    return -4;
+  dim3 grid((a.nq + 2 * TILE - 1) / (2 * TILE), a.heads, a.batch);
+  k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
+                                                   a.scale_log2, d_status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace exn

@@ -1,0 +1,1270 @@
+// dit.cpp -- the host side of libexn_b200.so: the C ABI of include/exn_b200.h.
+//
+// It does what ex-nihilo's src/cuda-dit.lisp does around its kernels --
+// weights checked and uploaded (upload-dit :52-86, open-dit
+// src/weights.lisp:47-61), one step's schedule (dit-velocity :137-243), the
+// prompt K/V kept under a key (:44-50, 148, 207-218, 232-233), buffers freed
+// (dit-release :99-108) -- and the step loop of src/generate.lisp:133-135,
+// with these B200-first differences:
+//   * weights live in HBM as bf16, dequantised once from Q8_0 (the values a
+//     dequantising GEMM would feed the tensor cores); to_q/to_k/to_v are one
+//     [3W x W] matrix and gate_up is interleaved by 128 rows so one 256-wide
+//     tile holds matching gate and up columns;
+//   * the latent, context, RoPE table and timestep embedding stay on the
+//     device; the Euler update is fused into proj_out's epilogue;
+//   * each layer's K/V buffer holds the whole sequence, so the prompt rows
+//     persist across steps without the reference's copies;
+//   * B independent pictures run as one batch of rows.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/exn_b200.h"
+#include "../../include/exn_b200_testing.h"
+#include "exn_internal.h"
+#include "gguf.h"
+
+using namespace exn;
+
+namespace {
+
+thread_local std::string g_open_error;
+const char* kPrefix = "model.diffusion_model.";
+
+struct TensorSpec {
+  std::string name;
+  std::vector<int64_t> dims;  // ggml order
+};
+
+// dit-expected, src/weights.lisp:22-45
+std::vector<TensorSpec> expected_tensors(const exn_config& c) {
+  const int64_t w = c.width, f = c.ffn;
+  std::vector<TensorSpec> v = {
+      {"img_in.weight", {c.latent, w}},
+      {"txt_in.text_norm.weight", {c.context}},
+      {"txt_in.in_layer.weight", {c.context, w}},
+      {"txt_in.out_layer.weight", {w, w}},
+      {"time_text_embed.timestep_embedder.linear_1.weight", {c.freq, w}},
+      {"time_text_embed.timestep_embedder.linear_2.weight", {w, w}},
+      {"modulation.1.weight", {w, 4 * w}},
+      {"norm_out.linear.weight", {w, w}},
+      {"proj_out.weight", {w, c.latent}},
+  };
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string b = "transformer_blocks." + std::to_string(i) + ".";
+    v.push_back({b + "attn.norm_q.weight", {c.head_dim}});
+    v.push_back({b + "attn.norm_k.weight", {c.head_dim}});
+    v.push_back({b + "attn.to_q.weight", {w, w}});
+    v.push_back({b + "attn.to_k.weight", {w, w}});
+    v.push_back({b + "attn.to_v.weight", {w, w}});
+    v.push_back({b + "attn.to_out.0.weight", {w, w}});
+    v.push_back({b + "img_mlp.gate_up.weight", {w, 2 * f}});
+    v.push_back({b + "img_mlp.out.weight", {f, w}});
+  }
+  return v;
+}
+
+std::string dims_str(const std::vector<int64_t>& d) {
+  std::string s = "(";
+  for (size_t i = 0; i < d.size(); ++i) s += (i ? " " : "") + std::to_string(d[i]);
+  return s + ")";
+}
+
+struct GemvW {
+  int kind = W_Q8;
+  void* w = nullptr;   // int8 qs / bf16 / f32 [out][in]
+  __half* d = nullptr; // Q8 scales [out][in/32]
+};
+
+struct Profile {
+  bool on = false;
+  std::vector<std::pair<cudaEvent_t, int>> marks;  // event, category of the work after it
+};
+
+}  // namespace
+
+struct exn_handle {
+  exn_config cfg{};
+  int sms = 0;
+  cudaStream_t st = nullptr;
+  std::string err;
+  int* d_status = nullptr;
+  std::vector<TensorSpec> spec;
+  std::map<std::string, int> index;
+  std::vector<char> loaded;
+  size_t n_loaded = 0;
+
+  // weights (one slab)
+  void* slab = nullptr;
+  size_t slab_bytes = 0;
+  bf16 *w_qkv = nullptr, *w_out = nullptr, *w_gu = nullptr, *w_down = nullptr;
+  bf16 *w_txt_in = nullptr, *w_txt_out = nullptr, *w_img_in = nullptr, *w_proj = nullptr;
+  float *norm_q = nullptr, *norm_k = nullptr, *txt_norm = nullptr;
+  GemvW lin1, lin2, mod, nout;
+  std::vector<void*> extra_allocs;
+
+  // step buffers
+  void* act = nullptr;
+  size_t act_bytes = 0;
+  int cap_batch = 0, cap_rows = 0, cap_l = 0, cap_p = 0, cap_nimg = 0, cap_nref = 0;
+  float* x = nullptr;
+  bf16 *y = nullptr, *q = nullptr, *att = nullptr, *ff = nullptr, *ctxn = nullptr, *tin = nullptr;
+  bf16 *lat_rows = nullptr, *ref_rows = nullptr;
+  float *ctx_dev = nullptr, *lat_dev = nullptr, *ref_dev = nullptr, *vout = nullptr;
+  float2* rope = nullptr;
+  float *emb = nullptr, *e1 = nullptr, *e2 = nullptr, *modv = nullptr, *sc = nullptr;
+  bf16* kv = nullptr;          // [layers][2][batch][cap_l][width]
+  size_t kv_bytes = 0;
+  int kv_batch = 0, kv_l = 0;
+
+  // the kept prompt
+  uint64_t prefix_key = 0;
+  int prefix_len = 0;
+  bool prefix_valid = false;
+
+  // debugging
+  float* trace_host = nullptr;
+  size_t trace_floats = 0;
+  Profile prof;
+  double last_ms[3] = {0, 0, 0};
+  long long launches = 0;  // kernels of this library queued by the step code since open
+};
+
+namespace {
+
+int fail(exn_handle* h, int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (h)
+    h->err = buf;
+  else
+    g_open_error = buf;
+  return code;
+}
+
+#define CK(call)                                                                                    \
+  do {                                                                                              \
+    cudaError_t e_ = (call);                                                                        \
+    if (e_ != cudaSuccess)                                                                          \
+      return fail(h, e_ == cudaErrorMemoryAllocation ? EXN_ENOMEM : EXN_ECUDA, "%s: %s (%s:%d)", #call, \
+                  cudaGetErrorString(e_), __FILE__, __LINE__);                                      \
+  } while (0)
+
+#define CKL(call)                                                                      \
+  do {                                                                                 \
+    int r_ = (call);                                                                   \
+    if (r_ != 0) return fail(h, EXN_ECUDA, "%s failed (%d) at %s:%d", #call, r_, __FILE__, __LINE__); \
+  } while (0)
+
+int use_device(exn_handle* h) {
+  CK(cudaSetDevice(h->cfg.device));
+  return EXN_OK;
+}
+
+inline size_t al(size_t n) { return (n + 255) & ~size_t(255); }
+
+// ---------------------------------------------------------------------------- weights
+
+int alloc_weights(exn_handle* h) {
+  const exn_config& c = h->cfg;
+  const size_t W = c.width, F = c.ffn, L = c.layers;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += al(bytes);
+    return o;
+  };
+  const size_t o_qkv = take(L * 3 * W * W * 2), o_out = take(L * W * W * 2), o_gu = take(L * 2 * F * W * 2),
+               o_down = take(L * W * F * 2), o_tin = take(W * c.context * 2), o_tout = take(W * W * 2),
+               o_img = take(W * c.latent * 2), o_proj = take(size_t(c.latent) * W * 2),
+               o_nq = take(L * c.head_dim * 4), o_nk = take(L * c.head_dim * 4), o_tn = take(size_t(c.context) * 4);
+  h->slab_bytes = off;
+  CK(cudaMalloc(&h->slab, off));
+  char* b = static_cast<char*>(h->slab);
+  h->w_qkv = reinterpret_cast<bf16*>(b + o_qkv);
+  h->w_out = reinterpret_cast<bf16*>(b + o_out);
+  h->w_gu = reinterpret_cast<bf16*>(b + o_gu);
+  h->w_down = reinterpret_cast<bf16*>(b + o_down);
+  h->w_txt_in = reinterpret_cast<bf16*>(b + o_tin);
+  h->w_txt_out = reinterpret_cast<bf16*>(b + o_tout);
+  h->w_img_in = reinterpret_cast<bf16*>(b + o_img);
+  h->w_proj = reinterpret_cast<bf16*>(b + o_proj);
+  h->norm_q = reinterpret_cast<float*>(b + o_nq);
+  h->norm_k = reinterpret_cast<float*>(b + o_nk);
+  h->txt_norm = reinterpret_cast<float*>(b + o_tn);
+  return EXN_OK;
+}
+
+// where a 2-D tensor goes: a bf16 GEMM slot (dst, row0, interleave) or a GEMV
+struct Route {
+  bf16* dst = nullptr;
+  long long row0 = 0;
+  int ilv = 0;
+  GemvW* gemv = nullptr;
+  float* vec = nullptr;  // 1-D
+  bool plus_one = false; // txt_in.text_norm: used as 1 + w
+};
+
+Route route(exn_handle* h, const std::string& name) {
+  const exn_config& c = h->cfg;
+  const long long W = c.width, F = c.ffn;
+  Route r;
+  if (name == "img_in.weight") r.dst = h->w_img_in;
+  else if (name == "txt_in.text_norm.weight") { r.vec = h->txt_norm; r.plus_one = true; }
+  else if (name == "txt_in.in_layer.weight") r.dst = h->w_txt_in;
+  else if (name == "txt_in.out_layer.weight") r.dst = h->w_txt_out;
+  else if (name == "time_text_embed.timestep_embedder.linear_1.weight") r.gemv = &h->lin1;
+  else if (name == "time_text_embed.timestep_embedder.linear_2.weight") r.gemv = &h->lin2;
+  else if (name == "modulation.1.weight") r.gemv = &h->mod;
+  else if (name == "norm_out.linear.weight") r.gemv = &h->nout;
+  else if (name == "proj_out.weight") r.dst = h->w_proj;
+  else {
+    int il = -1;
+    char part[128] = {0};
+    if (sscanf(name.c_str(), "transformer_blocks.%d.%127s", &il, part) == 2 && il >= 0 && il < c.layers) {
+      const std::string p = part;
+      if (p == "attn.norm_q.weight") r.vec = h->norm_q + il * c.head_dim;
+      else if (p == "attn.norm_k.weight") r.vec = h->norm_k + il * c.head_dim;
+      else if (p == "attn.to_q.weight") { r.dst = h->w_qkv; r.row0 = il * 3 * W; }
+      else if (p == "attn.to_k.weight") { r.dst = h->w_qkv; r.row0 = il * 3 * W + W; }
+      else if (p == "attn.to_v.weight") { r.dst = h->w_qkv; r.row0 = il * 3 * W + 2 * W; }
+      else if (p == "attn.to_out.0.weight") { r.dst = h->w_out; r.row0 = il * W; }
+      else if (p == "img_mlp.gate_up.weight") { r.dst = h->w_gu; r.row0 = il * 2 * F; r.ilv = static_cast<int>(F); }
+      else if (p == "img_mlp.out.weight") { r.dst = h->w_down; r.row0 = il * W; }
+    }
+  }
+  return r;
+}
+
+// Place one tensor whose GGUF bytes are on the device (RAW).  Q8_0 matrices
+// become bf16 (GEMM) or stay Q8_0 (GEMV); f32/f16/bf16 are converted.
+int place(exn_handle* h, int idx, int type, const void* raw, void* scratch) {
+  const TensorSpec& s = h->spec[idx];
+  Route r = route(h, s.name);
+  const long long cols = s.dims[0];
+  const long long rows = s.dims.size() > 1 ? s.dims[1] : 1;
+  const long long n = rows * cols;
+  if (r.vec) {
+    if (type == GGML_F32) CK(cudaMemcpyAsync(r.vec, raw, n * 4, cudaMemcpyDeviceToDevice, h->st));
+    else if (type == GGML_F16) f16_to_f32_launch(static_cast<const __half*>(raw), r.vec, n, h->st);
+    else if (type == GGML_BF16) bf16_to_f32_launch(static_cast<const bf16*>(raw), r.vec, n, h->st);
+    else return fail(h, EXN_EUNSUPPORTED, "%s: ggml type %d for a vector", s.name.c_str(), type);
+    if (r.plus_one) add_scalar_launch(r.vec, n, 1.f, h->st);
+  } else if (r.gemv) {
+    GemvW& g = *r.gemv;
+    if (type == GGML_Q8_0) {
+      void* qs = nullptr;
+      void* d = nullptr;
+      CK(cudaMalloc(&qs, n));
+      h->extra_allocs.push_back(qs);
+      CK(cudaMalloc(&d, (n / 32) * 2));
+      h->extra_allocs.push_back(d);
+      q8_raw_split_launch(static_cast<const uint8_t*>(raw), static_cast<int8_t*>(qs), static_cast<__half*>(d), n / 32,
+                          h->st);
+      g.kind = W_Q8;
+      g.w = qs;
+      g.d = static_cast<__half*>(d);
+    } else if (type == GGML_BF16) {
+      void* w = nullptr;
+      CK(cudaMalloc(&w, n * 2));
+      h->extra_allocs.push_back(w);
+      CK(cudaMemcpyAsync(w, raw, n * 2, cudaMemcpyDeviceToDevice, h->st));
+      g.kind = W_BF16;
+      g.w = w;
+    } else if (type == GGML_F32 || type == GGML_F16) {
+      void* w = nullptr;
+      CK(cudaMalloc(&w, n * 4));
+      h->extra_allocs.push_back(w);
+      if (type == GGML_F32) CK(cudaMemcpyAsync(w, raw, n * 4, cudaMemcpyDeviceToDevice, h->st));
+      else f16_to_f32_launch(static_cast<const __half*>(raw), static_cast<float*>(w), n, h->st);
+      g.kind = W_F32;
+      g.w = w;
+    } else {
+      return fail(h, EXN_EUNSUPPORTED, "%s: ggml type %d", s.name.c_str(), type);
+    }
+  } else if (r.dst) {
+    if (type == GGML_Q8_0) {
+      q8_raw_to_bf16_launch(static_cast<const uint8_t*>(raw), r.dst, rows, static_cast<int>(cols), r.row0, r.ilv, h->st);
+    } else if (type == GGML_BF16) {
+      bf16_rows_launch(static_cast<const bf16*>(raw), r.dst, rows, static_cast<int>(cols), r.row0, r.ilv, h->st);
+    } else if (type == GGML_F32) {
+      f32_to_bf16_rows_launch(static_cast<const float*>(raw), r.dst, rows, static_cast<int>(cols), r.row0, r.ilv, h->st);
+    } else if (type == GGML_F16) {
+      float* f = static_cast<float*>(scratch);
+      f16_to_f32_launch(static_cast<const __half*>(raw), f, n, h->st);
+      f32_to_bf16_rows_launch(f, r.dst, rows, static_cast<int>(cols), r.row0, r.ilv, h->st);
+    } else {
+      return fail(h, EXN_EUNSUPPORTED, "%s: ggml type %d", s.name.c_str(), type);
+    }
+  } else {
+    return fail(h, EXN_EINVAL, "no place for tensor %s", s.name.c_str());
+  }
+  CK(cudaGetLastError());
+  if (!h->loaded[idx]) {
+    h->loaded[idx] = 1;
+    ++h->n_loaded;
+  }
+  return EXN_OK;
+}
+
+int check_tensor(exn_handle* h, const std::string& name, int type, const std::vector<int64_t>& dims, int* idx) {
+  auto it = h->index.find(name);
+  if (it == h->index.end()) return fail(h, EXN_ESHAPE, "%s: not a tensor of the DiT", name.c_str());
+  const TensorSpec& s = h->spec[it->second];
+  if (s.dims != dims)
+    return fail(h, EXN_ESHAPE, "%s is %s, not %s", name.c_str(), dims_str(dims).c_str(), dims_str(s.dims).c_str());
+  if (type != GGML_F32 && type != GGML_F16 && type != GGML_BF16 && type != GGML_Q8_0)
+    return fail(h, EXN_EUNSUPPORTED, "%s: ggml type %d not handled", name.c_str(), type);
+  if (type == GGML_Q8_0 && dims.size() == 1)
+    return fail(h, EXN_EUNSUPPORTED, "%s: a Q8_0 vector", name.c_str());
+  *idx = it->second;
+  return EXN_OK;
+}
+
+// ---------------------------------------------------------------------------- step buffers
+
+int ensure_buffers(exn_handle* h, int batch, int n, int l, int ptext, int nimg, int nref) {
+  const exn_config& c = h->cfg;
+  const size_t W = c.width;
+  // per-step activations
+  if (batch > h->cap_batch || n > h->cap_rows || l > h->cap_l || ptext > h->cap_p || nimg > h->cap_nimg ||
+      nref > h->cap_nref) {
+    const int B = std::max(batch, h->cap_batch), R = std::max(n, h->cap_rows), Lc = std::max(l, h->cap_l);
+    const int P = std::max(ptext, h->cap_p), NI = std::max(nimg, h->cap_nimg), NR = std::max(nref, h->cap_nref);
+    const size_t rows = static_cast<size_t>(B) * R;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+      size_t o = off;
+      off += al(bytes);
+      return o;
+    };
+    const size_t ox = take(rows * W * 4), oy = take(rows * W * 2), oq = take(rows * W * 2), oa = take(rows * W * 2),
+                 of = take(rows * c.ffn * 2), ocn = take(size_t(B) * P * c.context * 2),
+                 oti = take(size_t(B) * P * W * 2), olr = take(size_t(B) * NI * c.latent * 2),
+                 orr = take(size_t(B) * std::max(NR, 1) * c.latent * 2), ocd = take(size_t(B) * P * c.context * 4),
+                 old = take(size_t(B) * NI * c.latent * 4), ord = take(size_t(B) * std::max(NR, 1) * c.latent * 4),
+                 ov = take(size_t(B) * NI * c.latent * 4), orp = take(size_t(Lc) * 64 * 8),
+                 oe = take(2 * c.freq * 4), oe1 = take(2 * W * 4), oe2 = take(2 * W * 4), om = take(8 * W * 4),
+                 osc = take(W * 4);
+    if (h->act) cudaFree(h->act);
+    h->act = nullptr;
+    CK(cudaMalloc(&h->act, off));
+    h->act_bytes = off;
+    char* b = static_cast<char*>(h->act);
+    h->x = reinterpret_cast<float*>(b + ox);
+    h->y = reinterpret_cast<bf16*>(b + oy);
+    h->q = reinterpret_cast<bf16*>(b + oq);
+    h->att = reinterpret_cast<bf16*>(b + oa);
+    h->ff = reinterpret_cast<bf16*>(b + of);
+    h->ctxn = reinterpret_cast<bf16*>(b + ocn);
+    h->tin = reinterpret_cast<bf16*>(b + oti);
+    h->lat_rows = reinterpret_cast<bf16*>(b + olr);
+    h->ref_rows = reinterpret_cast<bf16*>(b + orr);
+    h->ctx_dev = reinterpret_cast<float*>(b + ocd);
+    h->lat_dev = reinterpret_cast<float*>(b + old);
+    h->ref_dev = reinterpret_cast<float*>(b + ord);
+    h->vout = reinterpret_cast<float*>(b + ov);
+    h->rope = reinterpret_cast<float2*>(b + orp);
+    h->emb = reinterpret_cast<float*>(b + oe);
+    h->e1 = reinterpret_cast<float*>(b + oe1);
+    h->e2 = reinterpret_cast<float*>(b + oe2);
+    h->modv = reinterpret_cast<float*>(b + om);
+    h->sc = reinterpret_cast<float*>(b + osc);
+    h->cap_batch = B;
+    h->cap_rows = R;
+    h->cap_l = Lc;
+    h->cap_p = P;
+    h->cap_nimg = NI;
+    h->cap_nref = NR;
+  }
+  // K/V: [layers][2][batch][kv_l][W]; grown keeping the kept prompt rows
+  if (batch != h->kv_batch || l > h->kv_l) {
+    const int Lk = std::max(l, h->kv_l);
+    const size_t bytes = static_cast<size_t>(c.layers) * 2 * batch * Lk * W * 2;
+    bf16* nk = nullptr;
+    CK(cudaMalloc(&nk, bytes));
+    if (h->kv && h->prefix_valid && batch == h->kv_batch && h->prefix_len > 0) {
+      for (int i = 0; i < c.layers * 2 * batch; ++i)
+        CK(cudaMemcpyAsync(nk + static_cast<size_t>(i) * Lk * W, h->kv + static_cast<size_t>(i) * h->kv_l * W,
+                           static_cast<size_t>(h->prefix_len) * W * 2, cudaMemcpyDeviceToDevice, h->st));
+    } else {
+      h->prefix_valid = false;
+      h->prefix_key = 0;
+    }
+    CK(cudaStreamSynchronize(h->st));
+    if (h->kv) cudaFree(h->kv);
+    h->kv = nk;
+    h->kv_bytes = bytes;
+    h->kv_batch = batch;
+    h->kv_l = Lk;
+  }
+  return EXN_OK;
+}
+
+void free_buffers(exn_handle* h) {
+  if (h->act) cudaFree(h->act);
+  if (h->kv) cudaFree(h->kv);
+  h->act = nullptr;
+  h->kv = nullptr;
+  h->act_bytes = h->kv_bytes = 0;
+  h->cap_batch = h->cap_rows = h->cap_l = h->cap_p = h->cap_nimg = h->cap_nref = 0;
+  h->kv_batch = h->kv_l = 0;
+  h->prefix_valid = false;
+  h->prefix_key = 0;
+  h->prefix_len = 0;
+}
+
+// ---------------------------------------------------------------------------- profiling
+
+void prof_mark(exn_handle* h, int cat) {
+  if (!h->prof.on) return;
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, h->st);
+  h->prof.marks.push_back({e, cat});
+}
+
+void prof_collect(exn_handle* h) {
+  if (!h->prof.on || h->prof.marks.size() < 2) return;
+  cudaEventSynchronize(h->prof.marks.back().first);
+  double acc[3] = {0, 0, 0};
+  for (size_t i = 0; i + 1 < h->prof.marks.size(); ++i) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, h->prof.marks[i].first, h->prof.marks[i + 1].first);
+    acc[h->prof.marks[i].second] += ms;
+  }
+  for (auto& m : h->prof.marks) cudaEventDestroy(m.first);
+  h->prof.marks.clear();
+  for (int i = 0; i < 3; ++i) h->last_ms[i] = acc[i];
+}
+
+// ---------------------------------------------------------------------------- one step
+
+struct StepIn {
+  int batch = 1, ptext = 0, nref = 0, a = 0, rh = 0, rw = 0, hh = 0, ww = 0;
+  double sigma = 0;
+  bool cached = false;
+  const float* ctx = nullptr;   // device [B][ptext][context]
+  const float* ref = nullptr;   // device [B][64][nref]
+  const float* lat = nullptr;   // device [B][64][nimg]
+  float* z = nullptr;           // device: z += dsigma * v
+  float dsigma = 0.f;
+  float* v = nullptr;           // device: v out
+};
+
+int gemm(exn_handle* h, const bf16* a, long long lda, const bf16* b, long long ldb, int M, int N, int K, int epi,
+         const GemmEpi& ep) {
+  GemmArgs g;
+  g.a = a;
+  g.lda = lda;
+  g.b = b;
+  g.ldb = ldb;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = epi;
+  g.ep = ep;
+  const int r = gemm_launch(g, h->d_status, h->sms, h->st);
+  if (r) return fail(h, EXN_ECUDA, "GEMM %dx%dx%d (epilogue %d) launch failed: %d", M, N, K, epi, r);
+  return EXN_OK;
+}
+
+int run_step(exn_handle* h, const StepIn& in) {
+  const exn_config& c = h->cfg;
+  // kernels this step queues (timestep 5, inputs 2 or 5 (+2 with a reference), RoPE 1, 7 a block, final 2)
+  h->launches += 5 + 2 + 1 + 7LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
+  const int W = c.width, B = in.batch;
+  const int p = in.ptext + in.nref, nimg = in.hh * in.ww;
+  const int n0 = in.cached ? p : 0, n = in.cached ? nimg : p + nimg, L = p + nimg;
+  const int b0 = in.nref ? in.a : 0, b1 = in.nref ? in.a + in.nref : 0;
+  int rc;
+  if ((rc = ensure_buffers(h, B, n, L, in.ptext, nimg, in.nref))) return rc;
+  const size_t kv_layer = static_cast<size_t>(2) * B * h->kv_l * W;
+  const long long kv_sample = static_cast<long long>(h->kv_l) * W;
+
+  prof_mark(h, 2);
+  // timestep: emb(t), emb(0) -> linear_1, SiLU -> linear_2, SiLU -> modulation (gates tanh'd), norm_out (row 0)
+  temb_launch(h->emb, in.sigma, c.freq, h->st);
+  gemv_launch(h->lin1.kind, h->lin1.w, h->lin1.d, h->emb, h->e1, 2, c.freq, W, 1, 0, h->st);
+  gemv_launch(h->lin2.kind, h->lin2.w, h->lin2.d, h->e1, h->e2, 2, W, W, 1, 0, h->st);
+  gemv_launch(h->mod.kind, h->mod.w, h->mod.d, h->e2, h->modv, 2, W, 4 * W, 2, W, h->st);
+  gemv_launch(h->nout.kind, h->nout.w, h->nout.d, h->e2, h->sc, 1, W, W, 0, 0, h->st);
+  // the prompt (and an edit's picture) through txt_in / img_in, first pass only
+  if (!in.cached && in.ptext > 0) {
+    rms_launch(in.ctx, h->txt_norm, h->ctxn, B * in.ptext, c.context, h->st);
+    prof_mark(h, 0);
+    GemmEpi e1;
+    e1.out = h->tin;
+    e1.ld_out = W;
+    if ((rc = gemm(h, h->ctxn, c.context, h->w_txt_in, c.context, B * in.ptext, W, c.context, EPI_GELU_BF16, e1)))
+      return rc;
+    GemmEpi e2;
+    e2.out = h->x;
+    e2.ld_out = W;
+    e2.seg_in = in.ptext;
+    e2.seg_out = n;
+    e2.off = 0;
+    e2.split_at = in.nref ? in.a : (1 << 30);
+    e2.split_gap = in.nref;
+    if ((rc = gemm(h, h->tin, W, h->w_txt_out, W, B * in.ptext, W, W, EPI_F32, e2))) return rc;
+  }
+  if (!in.cached) {
+    if (in.nref) {
+      prof_mark(h, 2);
+      latent_rows_launch(in.ref, h->ref_rows, B, c.latent, in.nref, h->st);
+      prof_mark(h, 0);
+      GemmEpi er;
+      er.out = h->x;
+      er.ld_out = W;
+      er.seg_in = in.nref;
+      er.seg_out = n;
+      er.off = in.a;
+      if ((rc = gemm(h, h->ref_rows, c.latent, h->w_img_in, c.latent, B * in.nref, W, c.latent, EPI_F32, er))) return rc;
+    }
+    prof_mark(h, 2);
+  }
+  latent_rows_launch(in.lat, h->lat_rows, B, c.latent, nimg, h->st);
+  prof_mark(h, 0);
+  {
+    GemmEpi ei;
+    ei.out = h->x;
+    ei.ld_out = W;
+    ei.seg_in = nimg;
+    ei.seg_out = n;
+    ei.off = p - n0;
+    if ((rc = gemm(h, h->lat_rows, c.latent, h->w_img_in, c.latent, B * nimg, W, c.latent, EPI_F32, ei))) return rc;
+  }
+  prof_mark(h, 2);
+  rope_table_launch(h->rope, 0, L, p, in.hh, in.ww, in.nref ? in.a : 0, in.nref ? in.rh : 0, in.nref ? in.rw : 0,
+                    h->st);
+  if (h->trace_host && !in.cached) {
+    CK(cudaStreamSynchronize(h->st));
+  }
+  size_t traced = 0;
+  auto trace = [&](const float* src, int rows) -> int {
+    if (!h->trace_host) return EXN_OK;
+    const size_t nf = static_cast<size_t>(rows) * W;
+    if (traced + nf > h->trace_floats) return EXN_OK;
+    CK(cudaMemcpyAsync(h->trace_host + traced, src, nf * 4, cudaMemcpyDeviceToHost, h->st));
+    CK(cudaStreamSynchronize(h->st));
+    traced += nf;
+    return EXN_OK;
+  };
+  if (h->trace_host && (rc = trace(h->x, B * n))) return rc;
+
+  const int rows = B * n;
+  for (int il = 0; il < c.layers; ++il) {
+    bf16* kl = h->kv + il * kv_layer;
+    bf16* vl = kl + static_cast<size_t>(B) * h->kv_l * W;
+    ln_mod_launch(h->x, h->y, h->modv + 0 * W, 4 * W, rows, W, n, n, 0, n0, p, 0, h->st);
+    prof_mark(h, 0);
+    GemmEpi eq;
+    eq.seg_in = n;
+    eq.n0 = n0;
+    eq.width = W;
+    eq.norm_q = h->norm_q + il * c.head_dim;
+    eq.norm_k = h->norm_k + il * c.head_dim;
+    eq.rope = h->rope;
+    eq.q = h->q;
+    eq.k = kl;
+    eq.v = vl;
+    eq.kv_sample_stride = kv_sample;
+    if ((rc = gemm(h, h->y, W, h->w_qkv + static_cast<size_t>(il) * 3 * W * W, W, rows, 3 * W, W, EPI_QKV, eq)))
+      return rc;
+    prof_mark(h, 1);
+    AttnArgs aa;
+    aa.q = h->q;
+    aa.k = kl;
+    aa.v = vl;
+    aa.out = h->att;
+    aa.batch = B;
+    aa.nq = n;
+    aa.q0 = n0;
+    aa.p = p;
+    aa.l = L;
+    aa.b0 = b0;
+    aa.b1 = b1;
+    aa.heads = W / 128;
+    aa.width = W;
+    aa.kv_rows = h->kv_l;
+    aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
+    prof_mark(h, 0);
+    GemmEpi eo;
+    eo.out = h->x;
+    eo.ld_out = W;
+    eo.seg_in = n;
+    eo.mod = h->modv + 1 * W;
+    eo.mod_stride = 4 * W;
+    eo.n0 = n0;
+    eo.p = p;
+    if ((rc = gemm(h, h->att, W, h->w_out + static_cast<size_t>(il) * W * W, W, rows, W, W, EPI_GATE_RESID, eo)))
+      return rc;
+    prof_mark(h, 2);
+    ln_mod_launch(h->x, h->y, h->modv + 2 * W, 4 * W, rows, W, n, n, 0, n0, p, 0, h->st);
+    prof_mark(h, 0);
+    GemmEpi eg;
+    eg.out = h->ff;
+    eg.ld_out = c.ffn;
+    if ((rc = gemm(h, h->y, W, h->w_gu + static_cast<size_t>(il) * 2 * c.ffn * W, W, rows, 2 * c.ffn, W, EPI_SWIGLU,
+                   eg)))
+      return rc;
+    GemmEpi ed = eo;
+    ed.mod = h->modv + 3 * W;
+    if ((rc = gemm(h, h->ff, c.ffn, h->w_down + static_cast<size_t>(il) * W * c.ffn, c.ffn, rows, W, c.ffn,
+                   EPI_GATE_RESID, ed)))
+      return rc;
+    prof_mark(h, 2);
+    if (h->trace_host && (rc = trace(h->x, rows))) return rc;
+  }
+  // the image rows: LayerNorm * (1 + sc), proj_out (+ the Euler update)
+  ln_mod_launch(h->x, h->y, h->sc, 0, B * nimg, W, nimg, n, p - n0, n0, p, 1, h->st);
+  prof_mark(h, 0);
+  GemmEpi ep;
+  ep.z = in.z;
+  ep.vout = in.v;
+  ep.dsigma = in.dsigma;
+  ep.nimg = nimg;
+  if ((rc = gemm(h, h->y, W, h->w_proj, W, B * nimg, c.latent, W, EPI_PROJ, ep))) return rc;
+  prof_mark(h, 2);
+  CK(cudaGetLastError());
+  return EXN_OK;
+}
+
+int check_status(exn_handle* h) {
+  CK(cudaStreamSynchronize(h->st));
+  int s = 0;
+  CK(cudaMemcpy(&s, h->d_status, sizeof s, cudaMemcpyDeviceToHost));
+  if (s) {
+    cudaMemset(h->d_status, 0, sizeof(int));
+    return fail(h, EXN_ETIMEOUT, "a kernel gave up waiting on its pipeline (status 0x%x)", s);
+  }
+  prof_collect(h);
+  return EXN_OK;
+}
+
+int check_step_args(exn_handle* h, int batch, int p, int hh, int ww, const exn_ref* ref) {
+  if (batch < 1) return fail(h, EXN_EINVAL, "batch %d", batch);
+  if (p < 0 || hh < 1 || ww < 1) return fail(h, EXN_EINVAL, "p %d, h %d, w %d", p, hh, ww);
+  if (ref && (ref->a < 0 || ref->a > p || ref->rh < 1 || ref->rw < 1 || !ref->latent))
+    return fail(h, EXN_EINVAL, "bad reference picture (a %d, %d x %d)", ref ? ref->a : 0, ref ? ref->rh : 0,
+                ref ? ref->rw : 0);
+  if (h->n_loaded != h->spec.size())
+    return fail(h, EXN_ENOWEIGHTS, "%zu of %zu tensors loaded", h->n_loaded, h->spec.size());
+  return EXN_OK;
+}
+
+// upload host inputs for a batch-1 call
+int upload_inputs(exn_handle* h, const float* context, int p, const float* latent, int hh, int ww, const exn_ref* ref,
+                  bool need_ctx) {
+  const exn_config& c = h->cfg;
+  const int nimg = hh * ww, nref = ref ? ref->rh * ref->rw : 0;
+  int rc;
+  if ((rc = ensure_buffers(h, 1, (p + nref + nimg), p + nref + nimg, p, nimg, nref))) return rc;
+  if (need_ctx && p) CK(cudaMemcpyAsync(h->ctx_dev, context, size_t(p) * c.context * 4, cudaMemcpyHostToDevice, h->st));
+  if (need_ctx && nref)
+    CK(cudaMemcpyAsync(h->ref_dev, ref->latent, size_t(nref) * c.latent * 4, cudaMemcpyHostToDevice, h->st));
+  if (latent) CK(cudaMemcpyAsync(h->lat_dev, latent, size_t(nimg) * c.latent * 4, cudaMemcpyHostToDevice, h->st));
+  return EXN_OK;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+
+extern "C" {
+
+int exn_abi_version(void) { return EXN_ABI_VERSION; }
+
+void exn_default_config(exn_config* cfg) {
+  if (!cfg) return;
+  cfg->width = 4096;
+  cfg->layers = 32;
+  cfg->ffn = 12288;
+  cfg->latent = 64;
+  cfg->context = 4096;
+  cfg->freq = 256;
+  cfg->head_dim = 128;
+  cfg->device = 0;
+}
+
+int exn_open(const exn_config* cfg, exn_handle** out) {
+  exn_handle* h = nullptr;
+  if (!out) return fail(nullptr, EXN_EINVAL, "exn_open: null handle pointer");
+  *out = nullptr;
+  if (!cfg) return fail(nullptr, EXN_EINVAL, "exn_open: null config");
+  const exn_config& c = *cfg;
+  if (c.head_dim != 128 || c.width <= 0 || c.width % 256 || c.ffn <= 0 || c.ffn % 128 || c.layers <= 0 ||
+      c.latent != 64 || c.context <= 0 || c.context % 64 || c.context > 4096 || c.width > 4096 || c.freq <= 0 ||
+      c.freq % 64 || c.freq > 4096)
+    return fail(nullptr, EXN_EINVAL,
+                "exn_open: unsupported shape (width %d, ffn %d, layers %d, latent %d, context %d, freq %d, head_dim %d)",
+                c.width, c.ffn, c.layers, c.latent, c.context, c.freq, c.head_dim);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev)
+    return fail(nullptr, EXN_ECUDA, "exn_open: no CUDA device %d", c.device);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess)
+    return fail(nullptr, EXN_ECUDA, "exn_open: cannot query device %d", c.device);
+  if (prop.major != 10)
+    return fail(nullptr, EXN_EUNSUPPORTED, "exn_open: device %d is sm_%d%d; this library is built for sm_100a",
+                c.device, prop.major, prop.minor);
+  h = new exn_handle();
+  h->cfg = c;
+  h->sms = prop.multiProcessorCount;
+  int rc;
+  if ((rc = use_device(h)) || (rc = [&]() -> int {
+        CK(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking));
+        CK(cudaMalloc(&h->d_status, sizeof(int)));
+        CK(cudaMemset(h->d_status, 0, sizeof(int)));
+        return EXN_OK;
+      }()) ||
+      (rc = alloc_weights(h))) {
+    g_open_error = h->err;
+    exn_close(h);
+    return rc;
+  }
+  h->spec = expected_tensors(c);
+  for (size_t i = 0; i < h->spec.size(); ++i) h->index[h->spec[i].name] = static_cast<int>(i);
+  h->loaded.assign(h->spec.size(), 0);
+  h->prof.on = std::getenv("EXN_PROFILE") != nullptr;
+  *out = h;
+  return EXN_OK;
+}
+
+void exn_close(exn_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->cfg.device);
+  if (h->st) cudaStreamSynchronize(h->st);
+  free_buffers(h);
+  for (void* p : h->extra_allocs) cudaFree(p);
+  if (h->slab) cudaFree(h->slab);
+  if (h->d_status) cudaFree(h->d_status);
+  for (auto& m : h->prof.marks) cudaEventDestroy(m.first);
+  if (h->st) cudaStreamDestroy(h->st);
+  delete h;
+}
+
+const char* exn_last_error(const exn_handle* h) { return h ? h->err.c_str() : g_open_error.c_str(); }
+
+static int check_gguf(const exn_config& cfg, const std::vector<TensorSpec>& spec, const GgufFile& g,
+                      const char* path, std::string& msg) {
+  std::vector<std::string> problems;
+  if (g.arch != "qwen_image") problems.push_back("architecture \"" + g.arch + "\", not \"qwen_image\"");
+  std::map<std::string, const GgufTensor*> byname;
+  for (const auto& t : g.tensors) byname[t.name] = &t;
+  for (const auto& s : spec) {
+    auto it = byname.find(kPrefix + s.name);
+    if (it == byname.end())
+      problems.push_back("missing " + s.name);
+    else if (it->second->dims != s.dims)
+      problems.push_back(s.name + " is " + dims_str(it->second->dims) + ", not " + dims_str(s.dims));
+  }
+  const long extra = static_cast<long>(g.tensors.size()) - static_cast<long>(spec.size());
+  if (extra != 0) problems.push_back(std::to_string(extra) + " tensors more than the model has");
+  if (problems.empty()) return EXN_OK;
+  msg = std::string(path) + ":";
+  for (const auto& p : problems) msg += "\n  " + p;
+  (void)cfg;
+  return EXN_ESHAPE;
+}
+
+int exn_check_gguf(const exn_config* cfg, const char* path, char* msg, size_t msg_len) {
+  std::string m;
+  int rc = EXN_OK;
+  if (!cfg || !path) {
+    m = "exn_check_gguf: null argument";
+    rc = EXN_EINVAL;
+  } else {
+    GgufFile g;
+    if (!g.open(path, m))
+      rc = EXN_EIO;
+    else
+      rc = check_gguf(*cfg, expected_tensors(*cfg), g, path, m);
+  }
+  if (msg && msg_len) {
+    std::strncpy(msg, m.c_str(), msg_len - 1);
+    msg[msg_len - 1] = 0;
+  }
+  return rc;
+}
+
+int exn_load_gguf(exn_handle* h, const char* path) {
+  if (!h || !path) return fail(h, EXN_EINVAL, "exn_load_gguf: null argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  GgufFile g;
+  std::string err;
+  if (!g.open(path, err)) return fail(h, EXN_EIO, "%s", err.c_str());
+  // open-dit: architecture, every expected tensor's presence and dims, nothing extra
+  if ((rc = check_gguf(h->cfg, h->spec, g, path, err))) return fail(h, rc, "%s", err.c_str());
+  // upload: a pinned staging buffer, the raw bytes to the device, converted in place
+  size_t maxb = 0;
+  for (const auto& t : g.tensors) {
+    if (!t.nbytes) return fail(h, EXN_EUNSUPPORTED, "%s: ggml type %d not handled", t.name.c_str(), t.type);
+    maxb = std::max(maxb, t.nbytes);
+  }
+  void* raw = nullptr;
+  void* scratch = nullptr;
+  void* pinned = nullptr;
+  const size_t chunk = 64ull << 20;
+  CK(cudaMalloc(&raw, maxb));
+  if (cudaMalloc(&scratch, maxb * 2) != cudaSuccess || cudaMallocHost(&pinned, 2 * chunk) != cudaSuccess) {
+    cudaFree(raw);
+    if (scratch) cudaFree(scratch);
+    return fail(h, EXN_ENOMEM, "exn_load_gguf: staging buffers");
+  }
+  cudaEvent_t ev[2];
+  cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming);
+  rc = EXN_OK;
+  int slot = 0;
+  for (const auto& t : g.tensors) {
+    int idx = -1;
+    if ((rc = check_tensor(h, t.name.substr(strlen(kPrefix)), t.type, t.dims, &idx))) break;
+    const uint8_t* src = g.data(t);
+    for (size_t o = 0; o < t.nbytes && rc == EXN_OK; o += chunk) {
+      const size_t nb = std::min(chunk, t.nbytes - o);
+      char* pb = static_cast<char*>(pinned) + slot * chunk;
+      cudaEventSynchronize(ev[slot]);
+      std::memcpy(pb, src + o, nb);
+      if (cudaMemcpyAsync(static_cast<char*>(raw) + o, pb, nb, cudaMemcpyHostToDevice, h->st) != cudaSuccess)
+        rc = fail(h, EXN_ECUDA, "upload of %s failed", t.name.c_str());
+      cudaEventRecord(ev[slot], h->st);
+      slot ^= 1;
+    }
+    if (rc) break;
+    if ((rc = place(h, idx, t.type, raw, scratch))) break;
+  }
+  cudaStreamSynchronize(h->st);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  cudaFreeHost(pinned);
+  cudaFree(scratch);
+  cudaFree(raw);
+  if (rc) return rc;
+  CK(cudaGetLastError());
+  return EXN_OK;
+}
+
+int exn_load_tensor(exn_handle* h, const char* name, int ggml_type, int n_dims, const int64_t* dims, const void* data,
+                    size_t nbytes) {
+  if (!h || !name || !dims || !data || n_dims < 1 || n_dims > 4) return fail(h, EXN_EINVAL, "exn_load_tensor: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  std::vector<int64_t> d(dims, dims + n_dims);
+  int idx = -1;
+  if ((rc = check_tensor(h, name, ggml_type, d, &idx))) return rc;
+  const size_t need = ggml_nbytes(ggml_type, d);
+  if (need != nbytes) return fail(h, EXN_EINVAL, "%s: %zu bytes, expected %zu", name, nbytes, need);
+  void* raw = nullptr;
+  void* scratch = nullptr;
+  CK(cudaMalloc(&raw, nbytes));
+  if (cudaMalloc(&scratch, nbytes * 2 + 256) != cudaSuccess) {
+    cudaFree(raw);
+    return fail(h, EXN_ENOMEM, "exn_load_tensor: scratch");
+  }
+  rc = EXN_OK;
+  if (cudaMemcpyAsync(raw, data, nbytes, cudaMemcpyHostToDevice, h->st) != cudaSuccess)
+    rc = fail(h, EXN_ECUDA, "exn_load_tensor: upload failed");
+  if (!rc) rc = place(h, idx, ggml_type, raw, scratch);
+  cudaStreamSynchronize(h->st);
+  cudaFree(raw);
+  cudaFree(scratch);
+  return rc;
+}
+
+int exn_load_synthetic(exn_handle* h, uint64_t seed) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_load_synthetic: null handle");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  const double ih_std = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  const double std_dev = 0.02 * std::sqrt(4096.0 / h->cfg.width);
+  const float scale = static_cast<float>(std_dev / ih_std);
+  size_t maxn = 0;
+  for (const auto& s : h->spec) {
+    size_t n = 1;
+    for (auto d : s.dims) n *= d;
+    maxn = std::max(maxn, n);
+  }
+  int8_t* qs = nullptr;
+  __half* d = nullptr;
+  float* f = nullptr;
+  CK(cudaMalloc(&qs, maxn));
+  CK(cudaMalloc(&d, maxn / 32 * 2 + 256));
+  CK(cudaMalloc(&f, maxn * 4));
+  rc = EXN_OK;
+  for (size_t i = 0; i < h->spec.size() && !rc; ++i) {
+    const TensorSpec& s = h->spec[i];
+    const long long cols = s.dims[0], rows = s.dims.size() > 1 ? s.dims[1] : 1, n = rows * cols;
+    if (s.dims.size() == 1) {
+      const bool tn = s.name == "txt_in.text_norm.weight";
+      synth_f32_launch(f, n, seed, static_cast<uint32_t>(i), scale, tn ? 0.f : 1.f, h->st);
+      rc = place(h, static_cast<int>(i), GGML_F32, f, nullptr);
+    } else {
+      synth_q8_launch(qs, d, n, seed, static_cast<uint32_t>(i), scale, h->st);
+      Route r = route(h, s.name);
+      if (r.gemv) {
+        void* wq = nullptr;
+        void* wd = nullptr;
+        if (cudaMalloc(&wq, n) != cudaSuccess || cudaMalloc(&wd, n / 32 * 2) != cudaSuccess) {
+          rc = fail(h, EXN_ENOMEM, "exn_load_synthetic: %s", s.name.c_str());
+          break;
+        }
+        h->extra_allocs.push_back(wq);
+        h->extra_allocs.push_back(wd);
+        cudaMemcpyAsync(wq, qs, n, cudaMemcpyDeviceToDevice, h->st);
+        cudaMemcpyAsync(wd, d, n / 32 * 2, cudaMemcpyDeviceToDevice, h->st);
+        r.gemv->kind = W_Q8;
+        r.gemv->w = wq;
+        r.gemv->d = static_cast<__half*>(wd);
+      } else {
+        q8_to_bf16_launch(qs, d, r.dst, rows, static_cast<int>(cols), r.row0, r.ilv, h->st);
+      }
+      if (!h->loaded[i]) {
+        h->loaded[i] = 1;
+        ++h->n_loaded;
+      }
+    }
+    if (cudaGetLastError() != cudaSuccess) rc = fail(h, EXN_ECUDA, "exn_load_synthetic: %s", s.name.c_str());
+  }
+  cudaStreamSynchronize(h->st);
+  cudaFree(qs);
+  cudaFree(d);
+  cudaFree(f);
+  return rc;
+}
+
+int exn_weights_ready(const exn_handle* h) {
+  if (!h) return EXN_EINVAL;
+  return h->n_loaded == h->spec.size() ? EXN_OK : EXN_ENOWEIGHTS;
+}
+
+int exn_velocity(exn_handle* h, const float* context, int p, const float* latent, int hh, int ww, double sigma,
+                 uint64_t prefix_key, const exn_ref* ref, float* v_out) {
+  if (!h || !latent || !v_out || (p > 0 && !context)) return fail(h, EXN_EINVAL, "exn_velocity: null argument");
+  int rc;
+  if ((rc = use_device(h)) || (rc = check_step_args(h, 1, p, hh, ww, ref))) return rc;
+  const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
+  const bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len &&
+                      h->kv_batch == 1;
+  if ((rc = upload_inputs(h, context, p, latent, hh, ww, ref, !cached))) return rc;
+  if (!cached) {
+    h->prefix_valid = false;
+    h->prefix_key = 0;
+  }
+  StepIn in;
+  in.ptext = p;
+  in.nref = nref;
+  in.a = ref ? ref->a : 0;
+  in.rh = ref ? ref->rh : 0;
+  in.rw = ref ? ref->rw : 0;
+  in.hh = hh;
+  in.ww = ww;
+  in.sigma = sigma;
+  in.cached = cached;
+  in.ctx = h->ctx_dev;
+  in.ref = h->ref_dev;
+  in.lat = h->lat_dev;
+  in.v = h->vout;
+  if ((rc = run_step(h, in))) return rc;
+  CK(cudaMemcpyAsync(v_out, h->vout, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
+  if ((rc = check_status(h))) return rc;
+  if (prefix_key && !cached) {
+    h->prefix_key = prefix_key;
+    h->prefix_len = pfx;
+    h->prefix_valid = true;
+  }
+  return EXN_OK;
+}
+
+int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, int ww, const double* sigmas, int nsig,
+                 uint64_t prefix_key, const exn_ref* ref) {
+  if (!h || !z || !sigmas || (p > 0 && !context)) return fail(h, EXN_EINVAL, "exn_generate: null argument");
+  if (nsig < 2) return fail(h, EXN_EINVAL, "exn_generate: %d sigmas", nsig);
+  int rc;
+  if ((rc = use_device(h)) || (rc = check_step_args(h, 1, p, hh, ww, ref))) return rc;
+  const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
+  bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len && h->kv_batch == 1;
+  if ((rc = upload_inputs(h, context, p, z, hh, ww, ref, true))) return rc;
+  for (int s = 0; s + 1 < nsig; ++s) {
+    if (!cached) {
+      h->prefix_valid = false;
+      h->prefix_key = 0;
+    }
+    StepIn in;
+    in.ptext = p;
+    in.nref = nref;
+    in.a = ref ? ref->a : 0;
+    in.rh = ref ? ref->rh : 0;
+    in.rw = ref ? ref->rw : 0;
+    in.hh = hh;
+    in.ww = ww;
+    in.sigma = sigmas[s];
+    in.cached = cached;
+    in.ctx = h->ctx_dev;
+    in.ref = h->ref_dev;
+    in.lat = h->lat_dev;
+    in.z = h->lat_dev;
+    in.dsigma = static_cast<float>(sigmas[s + 1] - sigmas[s]);
+    if ((rc = run_step(h, in))) return rc;
+    if (!cached && prefix_key) {
+      h->prefix_key = prefix_key;
+      h->prefix_len = pfx;
+      h->prefix_valid = true;
+      cached = true;
+    }
+  }
+  CK(cudaMemcpyAsync(z, h->lat_dev, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
+  if ((rc = check_status(h))) {
+    h->prefix_valid = false;
+    h->prefix_key = 0;
+    return rc;
+  }
+  return EXN_OK;
+}
+
+static int generate_dev(exn_handle* h, int batch, const float* d_ctx, int p, float* d_z, int hh, int ww,
+                        const double* sigmas, int nsig) {
+  int rc;
+  h->prefix_valid = false;
+  h->prefix_key = 0;
+  for (int s = 0; s + 1 < nsig; ++s) {
+    StepIn in;
+    in.batch = batch;
+    in.ptext = p;
+    in.hh = hh;
+    in.ww = ww;
+    in.sigma = sigmas[s];
+    in.cached = s > 0;
+    in.ctx = d_ctx;
+    in.lat = d_z;
+    in.z = d_z;
+    in.dsigma = static_cast<float>(sigmas[s + 1] - sigmas[s]);
+    if ((rc = run_step(h, in))) return rc;
+  }
+  return EXN_OK;
+}
+
+int exn_generate_batch(exn_handle* h, int batch, const float* contexts, int p, float* z, int hh, int ww,
+                       const double* sigmas, int nsig) {
+  if (!h || !z || !sigmas || (p > 0 && !contexts)) return fail(h, EXN_EINVAL, "exn_generate_batch: null argument");
+  if (nsig < 2) return fail(h, EXN_EINVAL, "exn_generate_batch: %d sigmas", nsig);
+  int rc;
+  if ((rc = use_device(h)) || (rc = check_step_args(h, batch, p, hh, ww, nullptr))) return rc;
+  const exn_config& c = h->cfg;
+  const int nimg = hh * ww;
+  if ((rc = ensure_buffers(h, batch, p + nimg, p + nimg, p, nimg, 0))) return rc;
+  CK(cudaMemcpyAsync(h->ctx_dev, contexts, size_t(batch) * p * c.context * 4, cudaMemcpyHostToDevice, h->st));
+  CK(cudaMemcpyAsync(h->lat_dev, z, size_t(batch) * nimg * c.latent * 4, cudaMemcpyHostToDevice, h->st));
+  if ((rc = generate_dev(h, batch, h->ctx_dev, p, h->lat_dev, hh, ww, sigmas, nsig))) return rc;
+  CK(cudaMemcpyAsync(z, h->lat_dev, size_t(batch) * nimg * c.latent * 4, cudaMemcpyDeviceToHost, h->st));
+  return check_status(h);
+}
+
+int exn_generate_device(exn_handle* h, int batch, const float* d_contexts, int p, float* d_z, int hh, int ww,
+                        const double* sigmas, int nsig, void* stream) {
+  if (!h || !d_z || !sigmas || (p > 0 && !d_contexts)) return fail(h, EXN_EINVAL, "exn_generate_device: null argument");
+  if (nsig < 2) return fail(h, EXN_EINVAL, "exn_generate_device: %d sigmas", nsig);
+  int rc;
+  if ((rc = use_device(h)) || (rc = check_step_args(h, batch, p, hh, ww, nullptr))) return rc;
+  const int nimg = hh * ww;
+  if ((rc = ensure_buffers(h, batch, p + nimg, p + nimg, p, nimg, 0))) return rc;
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  if (user) {  // order after the caller's stream, and the caller's stream after us
+    cudaEvent_t e;
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaEventRecord(e, user));
+    CK(cudaStreamWaitEvent(h->st, e, 0));
+    cudaEventDestroy(e);
+  }
+  if ((rc = generate_dev(h, batch, d_contexts, p, d_z, hh, ww, sigmas, nsig))) return rc;
+  if (user) {
+    cudaEvent_t e;
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaEventRecord(e, h->st));
+    CK(cudaStreamWaitEvent(user, e, 0));
+    cudaEventDestroy(e);
+  }
+  return EXN_OK;
+}
+
+int exn_sync(exn_handle* h) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_sync: null handle");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  return check_status(h);
+}
+
+int exn_release(exn_handle* h) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_release: null handle");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  CK(cudaStreamSynchronize(h->st));
+  free_buffers(h);
+  return EXN_OK;
+}
+
+// ---------------------------------------------------------------------------- testing entry points
+
+int exn_test_gemm(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k) {
+  if (!h || !a || !b || !c) return fail(h, EXN_EINVAL, "exn_test_gemm: null argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  GemmEpi e;
+  e.out = c;
+  e.ld_out = n;
+  if ((rc = gemm(h, static_cast<const bf16*>(a), k, static_cast<const bf16*>(b), k, m, n, k, EPI_F32, e))) return rc;
+  return check_status(h);
+}
+
+int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
+                       int q0, int p, int l, int b0, int b1, int heads, int kv_rows) {
+  if (!h || !q || !k || !v || !out) return fail(h, EXN_EINVAL, "exn_test_attention: null argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  AttnArgs aa;
+  aa.q = static_cast<const bf16*>(q);
+  aa.k = static_cast<const bf16*>(k);
+  aa.v = static_cast<const bf16*>(v);
+  aa.out = static_cast<bf16*>(out);
+  aa.batch = batch;
+  aa.nq = nq;
+  aa.q0 = q0;
+  aa.p = p;
+  aa.l = l;
+  aa.b0 = b0;
+  aa.b1 = b1;
+  aa.heads = heads;
+  aa.width = heads * 128;
+  aa.kv_rows = kv_rows;
+  aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+  if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_EINVAL, "attention launch failed: %d", rc);
+  return check_status(h);
+}
+
+int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, int n, int width, int n0, int p) {
+  if (!h || !x || !y || !mod) return fail(h, EXN_EINVAL, "exn_test_ln_mod: null argument");
+  if (width % 4 || width > 4096) return fail(h, EXN_EINVAL, "exn_test_ln_mod: width %d", width);
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  ln_mod_launch(x, static_cast<bf16*>(y), mod, width, n, width, n, n, 0, n0, p, 0, h->st);
+  CK(cudaGetLastError());
+  return check_status(h);
+}
+
+int exn_test_qkv(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p, int hh,
+                 int ww, int kv_rows) {
+  if (!h || !y || !q || !k || !v) return fail(h, EXN_EINVAL, "exn_test_qkv: null argument");
+  if (layer < 0 || layer >= h->cfg.layers || n0 + n > kv_rows) return fail(h, EXN_EINVAL, "exn_test_qkv: bad sizes");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  const int W = h->cfg.width, L = p + hh * ww;
+  if ((rc = ensure_buffers(h, 1, 1, L, 1, 1, 0))) return rc;
+  rope_table_launch(h->rope, 0, L, p, hh, ww, 0, 0, 0, h->st);
+  GemmEpi eq;
+  eq.seg_in = n;
+  eq.n0 = n0;
+  eq.width = W;
+  eq.norm_q = h->norm_q + layer * 128;
+  eq.norm_k = h->norm_k + layer * 128;
+  eq.rope = h->rope;
+  eq.q = static_cast<bf16*>(q);
+  eq.k = static_cast<bf16*>(k);
+  eq.v = static_cast<bf16*>(v);
+  eq.kv_sample_stride = static_cast<long long>(kv_rows) * W;
+  if ((rc = gemm(h, static_cast<const bf16*>(y), W, h->w_qkv + static_cast<size_t>(layer) * 3 * W * W, W, n, 3 * W, W,
+                 EPI_QKV, eq)))
+    return rc;
+  return check_status(h);
+}
+
+int exn_test_trace(exn_handle* h, float* host, size_t floats) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_trace: null handle");
+  h->trace_host = host;
+  h->trace_floats = host ? floats : 0;
+  return EXN_OK;
+}
+
+int exn_test_weight_bf16(exn_handle* h, const char* name, void* host_bf16, size_t elems) {
+  if (!h || !name || !host_bf16) return fail(h, EXN_EINVAL, "exn_test_weight_bf16: null argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  auto it = h->index.find(name);
+  if (it == h->index.end()) return fail(h, EXN_EINVAL, "no tensor %s", name);
+  const TensorSpec& s = h->spec[it->second];
+  if (s.dims.size() != 2) return fail(h, EXN_EINVAL, "%s is not a matrix", name);
+  const long long cols = s.dims[0], rows = s.dims[1];
+  if (elems != static_cast<size_t>(rows * cols)) return fail(h, EXN_EINVAL, "%s: %zu elements asked", name, elems);
+  Route r = route(h, s.name);
+  bf16* tmp = nullptr;
+  CK(cudaMalloc(&tmp, elems * 2));
+  if (r.gemv) {
+    if (r.gemv->kind == W_Q8)
+      q8_to_bf16_launch(static_cast<const int8_t*>(r.gemv->w), r.gemv->d, tmp, rows, static_cast<int>(cols), 0, 0, h->st);
+    else if (r.gemv->kind == W_BF16)
+      cudaMemcpyAsync(tmp, r.gemv->w, elems * 2, cudaMemcpyDeviceToDevice, h->st);
+    else
+      f32_to_bf16_rows_launch(static_cast<const float*>(r.gemv->w), tmp, rows, static_cast<int>(cols), 0, 0, h->st);
+    cudaMemcpyAsync(host_bf16, tmp, elems * 2, cudaMemcpyDeviceToHost, h->st);
+  } else {
+    // undo the interleave / fusion: copy row by row from the placed position
+    std::vector<uint16_t> all(elems);
+    for (long long rr = 0; rr < rows; ++rr) {
+      long long dr;
+      if (r.ilv > 0) {
+        const long long g = rr < r.ilv ? rr : rr - r.ilv;
+        dr = r.row0 + (g / 128) * 256 + (rr < r.ilv ? 0 : 128) + (g % 128);
+      } else {
+        dr = r.row0 + rr;
+      }
+      cudaMemcpyAsync(all.data() + rr * cols, r.dst + dr * cols, cols * 2, cudaMemcpyDeviceToHost, h->st);
+    }
+    cudaStreamSynchronize(h->st);
+    std::memcpy(host_bf16, all.data(), elems * 2);
+  }
+  cudaStreamSynchronize(h->st);
+  cudaFree(tmp);
+  CK(cudaGetLastError());
+  return EXN_OK;
+}
+
+int exn_test_synth_normal(exn_handle* h, float* d, int64_t n, uint64_t seed, uint32_t stream, double std_dev) {
+  if (!h || !d || n < 0) return fail(h, EXN_EINVAL, "exn_test_synth_normal: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  const double ih_std = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  synth_f32_launch(d, n, seed, stream, static_cast<float>(std_dev / ih_std), 0.f, h->st);
+  CK(cudaGetLastError());
+  return check_status(h);
+}
+
+int exn_test_profile(exn_handle* h, int on) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_profile: null handle");
+  h->prof.on = on != 0;
+  return EXN_OK;
+}
+
+long long exn_test_launch_count(const exn_handle* h) { return h ? h->launches : -1; }
+
+int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_last_profile: null handle");
+  if (gemm_ms) *gemm_ms = h->last_ms[0];
+  if (attn_ms) *attn_ms = h->last_ms[1];
+  if (other_ms) *other_ms = h->last_ms[2];
+  return EXN_OK;
+}
+
+}  // extern "C"

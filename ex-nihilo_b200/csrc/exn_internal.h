@@ -1,0 +1,119 @@
+// exn_internal.h -- declarations shared by the kernels (.cu) and the host
+// driver (dit.cpp).  Not part of the public C ABI (include/exn_b200.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace exn {
+
+typedef __nv_bfloat16 bf16;
+
+// What a GEMM's epilogue does with the fp32 accumulator tile.
+enum EpiKind : int {
+  EPI_F32 = 0,         // out f32 at the mapped row
+  EPI_BF16 = 1,        // out bf16 at the mapped row
+  EPI_GELU_BF16 = 2,   // out bf16 = gelu_tanh(acc)                          (txt_in.in_layer)
+  EPI_QKV = 3,         // q/k: per-head RMSNorm * w, RoPE; v: as is -> bf16  (fused to_q/to_k/to_v)
+  EPI_GATE_RESID = 4,  // x[row] += tanh(gate)[mod row] * acc, f32           (to_out.0, img_mlp.out)
+  EPI_SWIGLU = 5,      // out bf16 = silu(gate) * up, gate/up interleaved by 128 columns (img_mlp.gate_up)
+  EPI_PROJ = 6,        // v channel-major and/or z += dsigma * v              (proj_out)
+};
+
+// GEMM row r maps to output row
+//   (r / seg_in) * seg_out + off + t + (t >= split_at ? split_gap : 0),  t = r % seg_in
+struct GemmEpi {
+  void* out = nullptr;
+  long long ld_out = 0;
+  int seg_in = 1 << 30, seg_out = 0, off = 0, split_at = 1 << 30, split_gap = 0;
+  // modulation rows [2][mod_stride]: row 0 (from t) for image rows, row 1 (from 0) for prompt rows;
+  // a row t of a sample is a prompt row when n0 + t < p
+  const float* mod = nullptr;
+  int mod_stride = 0, n0 = 0, p = 0;
+  // EPI_QKV
+  int width = 0;
+  const float* norm_q = nullptr;
+  const float* norm_k = nullptr;
+  const float2* rope = nullptr;  // [sequence row][64] (cos, sin)
+  bf16* q = nullptr;
+  bf16* k = nullptr;
+  bf16* v = nullptr;
+  long long kv_sample_stride = 0;  // elements from one sample's K (V) rows to the next
+  // EPI_PROJ
+  float* z = nullptr;
+  float* vout = nullptr;
+  float dsigma = 0.f;
+  int nimg = 0;
+};
+
+struct GemmArgs {
+  const bf16* a = nullptr;  // [M][K], row stride lda elements
+  long long lda = 0;
+  const bf16* b = nullptr;  // [N][K], row stride ldb elements (a weight, out x in)
+  long long ldb = 0;
+  int M = 0, N = 0, K = 0;
+  int epi = EPI_F32;
+  GemmEpi ep;
+};
+
+// C = A B^T through the tcgen05 kernel.  0, or a cudaError_t / -1 (bad shape).
+int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st);
+
+struct AttnArgs {
+  const bf16* q = nullptr;   // [B][nq][width]
+  const bf16* k = nullptr;   // [B][kv_rows][width]: this layer's keys
+  const bf16* v = nullptr;
+  bf16* out = nullptr;       // [B][nq][width]
+  int batch = 1, nq = 0, q0 = 0, p = 0, l = 0, b0 = 0, b1 = 0;
+  int heads = 0, width = 0;
+  int kv_rows = 0;           // row capacity of one sample's K/V
+  float scale_log2 = 0.f;    // log2(e) / sqrt(128)
+};
+int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st);
+
+// --- memory-bound kernels (elementwise.cu) ---
+// y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.
+// single: one modulation row for every row (norm_out's scale).
+void ln_mod_launch(const float* x, bf16* y, const float* scale, int mod_stride, int rows, int width, int seg_in,
+                   int seg_out, int off, int n0, int p, int single, cudaStream_t st);
+// y = RMSNorm(x) * w (w already 1 + text_norm), bf16 out
+void rms_launch(const float* x, const float* w, bf16* y, int rows, int width, cudaStream_t st);
+// latent [B][C][n] f32 channel-major -> rows [B*n][C] bf16
+void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, int n, cudaStream_t st);
+// RoPE (cos, sin) of rows r0 .. r0+count of the sequence (host.lisp's positions), [count][64]
+void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, int ref_a, int ref_h, int ref_w,
+                       cudaStream_t st);
+// emb[2][freq]: timestep embedding of 1000*sigma and of 0
+void temb_launch(float* emb, double sigma, int freq, cudaStream_t st);
+// Weight kinds for the small GEMVs
+enum WKind : int { W_Q8 = 0, W_BF16 = 1, W_F32 = 2 };
+// y[m][out] = act(x[m][in] . W[out][in]); act 0 none, 1 silu, 2 tanh on columns of pieces 1 and 3 (of 4)
+void gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out,
+                 int act, int piece, cudaStream_t st);
+// GGUF Q8_0 blocks (34 B) -> bf16 rows, row r written at dst_row(r) (gate_up interleave when ilv > 0)
+void q8_raw_to_bf16_launch(const uint8_t* raw, bf16* dst, long long rows, int cols, long long row0, int ilv,
+                           cudaStream_t st);
+// GGUF Q8_0 blocks -> separate int8 qs and fp16 d
+void q8_raw_split_launch(const uint8_t* raw, int8_t* qs, __half* d, long long nblocks, cudaStream_t st);
+// f32 / bf16 / f16 rows -> bf16 rows (same permutation rules)
+void f32_to_bf16_rows_launch(const float* src, bf16* dst, long long rows, int cols, long long row0, int ilv,
+                             cudaStream_t st);
+void bf16_rows_launch(const bf16* src, bf16* dst, long long rows, int cols, long long row0, int ilv,
+                      cudaStream_t st);
+void f16_to_f32_launch(const __half* src, float* dst, long long n, cudaStream_t st);
+void bf16_to_f32_launch(const bf16* src, float* dst, long long n, cudaStream_t st);
+// synthetic Q8_0 tensor (the oracle's generator): qs int8 [n], d fp16 [n/32]
+void synth_q8_launch(int8_t* qs, __half* d, long long n, uint64_t seed, uint32_t stream, float scale,
+                     cudaStream_t st);
+// synthetic f32 vector: base + offset * scale
+void synth_f32_launch(float* v, long long n, uint64_t seed, uint32_t stream, float scale, float base,
+                      cudaStream_t st);
+// Q8 (qs, d) -> bf16 rows with the same permutation rules
+void q8_to_bf16_launch(const int8_t* qs, const __half* d, bf16* dst, long long rows, int cols, long long row0,
+                       int ilv, cudaStream_t st);
+void add_scalar_launch(float* v, long long n, float a, cudaStream_t st);
+
+}  // namespace exn

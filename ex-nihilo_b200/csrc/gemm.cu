@@ -1,0 +1,440 @@
+// gemm.cu -- the DiT's weight products on the 5th-generation tensor cores.
+//
+// C[M x N] = A[M x K] . B[N x K]^T with A the bf16 activations and B a bf16
+// weight (out x in, both K-contiguous: the "TN" case).  One persistent CTA
+// per SM walks output tiles of 128 x BN:
+//
+//   warp 0      TMA producer: A and B k-blocks of 64 into a STAGES-deep ring
+//               of 128-byte-swizzled shared memory tiles
+//   warp 1      MMA issuer: tcgen05.mma kind::f16 (M=128, N=BN, K=16) into
+//               one of two TMEM accumulators (2 x BN fp32 columns)
+//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (one row per
+//               thread) and the fused per-layer arithmetic of the DiT, while
+//               the MMA already fills the other accumulator
+//
+// The epilogues replace the reference's separate elementwise launches
+// (src/cuda/dit.cu: x_gate_add :34-41, x_qk_norm_rope :43-58, x_swiglu2
+// :186-192, x_gelu_tanh :194-199) and the host Euler update
+// (src/generate.lisp:135) that followed illatio's GEMMs (src/cuda-dit.lisp
+// :115-130).
+#include <mutex>
+
+#include "exn_device.cuh"
+#include "exn_internal.h"
+
+namespace exn {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+};
+
+__device__ __forceinline__ long long map_row(const GemmEpi& e, int r) {
+  const int b = r / e.seg_in, t = r - b * e.seg_in;
+  return static_cast<long long>(b) * e.seg_out + e.off + t + (t >= e.split_at ? e.split_gap : 0);
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  constexpr int GM = 16;  // 16 row blocks share each weight tile while it sits in L2
+  const int group = tile / (GM * num_n);
+  const int first = group * GM;
+  const int gm = min(GM, num_m - first);
+  const int in_g = tile - group * GM * num_n;
+  mb = first + in_g % gm;
+  nb = in_g / gm;
+}
+
+__device__ __forceinline__ float gelu_tanh(float v) {
+  return 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.f + expf(-g)); }
+
+__device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
+  uint4* o = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    o[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+}
+
+// ----------------------------------------------------------------------------- epilogues
+// TADDR: TMEM address of this warp's 32 lanes at the accumulator's column 0.
+// ROW: this thread's GEMM row; VALID: row < M; COL0: the tile's first column.
+
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, int col0, const GemmEpi& e) {
+  if constexpr (EPI == EPI_F32 || EPI == EPI_BF16 || EPI == EPI_GELU_BF16) {
+    const long long orow = valid ? map_row(e, row) : 0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      if (!valid) continue;
+      float f[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
+      if constexpr (EPI == EPI_F32) {
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + orow * e.ld_out + col0 + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
+      } else {
+        if constexpr (EPI == EPI_GELU_BF16) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = gelu_tanh(f[i]);
+        }
+        store_bf16x32(static_cast<bf16*>(e.out) + orow * e.ld_out + col0 + c, f);
+      }
+    }
+  } else if constexpr (EPI == EPI_GATE_RESID) {
+    const int t = row % e.seg_in;
+    const float* g = e.mod + (e.n0 + t < e.p ? e.mod_stride : 0) + col0;
+    float* x = static_cast<float*>(e.out) + static_cast<long long>(row) * e.ld_out + col0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      if (!valid) continue;
+      float4* xp = reinterpret_cast<float4*>(x + c);
+      const float4* gp = reinterpret_cast<const float4*>(g + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 xv = xp[i];
+        const float4 gv = __ldg(gp + i);
+        xv.x += gv.x * __uint_as_float(r[4 * i]);
+        xv.y += gv.y * __uint_as_float(r[4 * i + 1]);
+        xv.z += gv.z * __uint_as_float(r[4 * i + 2]);
+        xv.w += gv.w * __uint_as_float(r[4 * i + 3]);
+        xp[i] = xv;
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    static_assert(BN == 256, "SwiGLU tiles hold 128 gate and 128 up columns");
+    bf16* o = static_cast<bf16*>(e.out) + static_cast<long long>(row) * e.ld_out + col0 / 2;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c, rg);
+      tmem_ld32(taddr + 128 + c, ru);
+      if (!valid) continue;
+      float f[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[i] = silu(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+      store_bf16x32(o + c, f);
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    static_assert(BN == 256, "QKV tiles hold two whole heads");
+    const int sec = col0 / e.width;            // 0 q, 1 k, 2 v
+    const int hc0 = col0 - sec * e.width;      // first column within q / k / v
+    const int t = row % e.seg_in, b = row / e.seg_in;
+    bf16* dst;
+    if (sec == 0)
+      dst = e.q + static_cast<long long>(row) * e.width + hc0;
+    else
+      dst = (sec == 1 ? e.k : e.v) + b * e.kv_sample_stride + static_cast<long long>(e.n0 + t) * e.width + hc0;
+    const float* nw = sec == 0 ? e.norm_q : e.norm_k;
+    const float2* cs = e.rope + static_cast<long long>(e.n0 + t) * 64;
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      float v[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + hh * 128 + c * 32, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      if (!valid) continue;
+      if (sec < 2) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
+        const float inv = rsqrtf(ss / 128.f + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float a = v[2 * j] * inv * __ldg(nw + 2 * j);
+          const float bq = v[2 * j + 1] * inv * __ldg(nw + 2 * j + 1);
+          const float2 r = __ldg(cs + j);
+          v[2 * j] = a * r.x - bq * r.y;
+          v[2 * j + 1] = a * r.y + bq * r.x;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) store_bf16x32(dst + hh * 128 + c * 32, v + c * 32);
+    }
+  } else if constexpr (EPI == EPI_PROJ) {
+    static_assert(BN == 64, "proj_out has the latent's 64 channels");
+    const int b = row / e.nimg, i = row - (row / e.nimg) * e.nimg;
+    const long long base = static_cast<long long>(b) * 64 * e.nimg + i;
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      if (!valid) continue;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const long long idx = base + static_cast<long long>(c + j) * e.nimg;
+        const float val = __uint_as_float(r[j]);
+        if (e.vout) e.vout[idx] = val;
+        if (e.z) e.z[idx] += e.dsigma * val;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- the kernel
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+           const GemmEpi ep, int* status) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = N / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_phase[C::STAGES];
+#pragma unroll
+      for (int s = 0; s < C::STAGES; ++s) last_phase[s] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          last_phase[stage] = static_cast<int>(phase);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // let the copies already issued land before the CTA leaves
+        volatile int no_abort = 0;
+        for (int s = 0; s < C::STAGES; ++s)
+          if (last_phase[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_phase[s]), &no_abort, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_ss(d_tmem, ad, bd, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // every MMA issued has finished before TMEM is released
+      umma_commit(done);
+      volatile int no_abort = 0;
+      mbar_wait(done, 0, &no_abort, nullptr, 0);
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
+      tc_fence_after();
+      const int row = mb * BM + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      epilogue<BN, EPI>(taddr, row, row < M, nb * BN, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map, 128-byte swizzle, zero fill out of bounds.  dims[0] is
+// the contiguous axis; strides (bytes) for dims 1..rank-1.
+int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                   const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i < rank - 1) s[i] = strides[i];
+  }
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+template <int BN, int EPI>
+static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  static bool attr = false;  // per instantiation; set before the first launch
+  if (!attr) {
+    if (cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  CUtensorMap ta, tb;
+  const uint64_t da[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(g.lda) * 2};
+  const uint32_t ba[2] = {BK, BM};
+  const uint64_t db[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(g.ldb) * 2};
+  const uint32_t bb[2] = {BK, BN};
+  if (make_tmap_bf16(&ta, g.a, 2, da, sa, ba) || make_tmap_bf16(&tb, g.b, 2, db, sb, bb)) return -4;
+  const int tiles = ((g.M + BM - 1) / BM) * (g.N / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  k_gemm<BN, EPI><<<grid, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, g.ep, d_status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK) return -1;
+  if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b)) & 15) return -1;
+  if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return -1;
+  switch (g.epi) {
+    case EPI_QKV:
+      if (g.N % 256 || g.ep.width % 256) return -1;
+      return launch_bn<256, EPI_QKV>(g, d_status, num_sms, st);
+    case EPI_SWIGLU:
+      if (g.N % 256) return -1;
+      return launch_bn<256, EPI_SWIGLU>(g, d_status, num_sms, st);
+    case EPI_PROJ:
+      if (g.N != 64) return -1;
+      return launch_bn<64, EPI_PROJ>(g, d_status, num_sms, st);
+    case EPI_GATE_RESID:
+      if (g.N % 256 == 0) return launch_bn<256, EPI_GATE_RESID>(g, d_status, num_sms, st);
+      if (g.N % 128 == 0) return launch_bn<128, EPI_GATE_RESID>(g, d_status, num_sms, st);
+      return -1;
+    case EPI_F32:
+      if (g.N % 256 == 0) return launch_bn<256, EPI_F32>(g, d_status, num_sms, st);
+      if (g.N % 64 == 0) return launch_bn<64, EPI_F32>(g, d_status, num_sms, st);
+      return -1;
+    case EPI_BF16:
+      if (g.N % 256 == 0) return launch_bn<256, EPI_BF16>(g, d_status, num_sms, st);
+      if (g.N % 64 == 0) return launch_bn<64, EPI_BF16>(g, d_status, num_sms, st);
+      return -1;
+    case EPI_GELU_BF16:
+      if (g.N % 256 == 0) return launch_bn<256, EPI_GELU_BF16>(g, d_status, num_sms, st);
+      return -1;
+  }
+  return -1;
+}
+
+}  // namespace exn

@@ -1,0 +1,288 @@
+"""Host-side mirror of ex-nihilo's DiT driver over libexn_b200.so.
+
+The reference drives its DiT from Common Lisp (SBCL, not available here)
+through three functions of src/cuda-dit.lisp and one loop of
+src/generate.lisp; this module keeps their names, arguments and error
+behaviour on top of the C ABI in include/exn_b200.h:
+
+    upload_dit(path, device=0)                       (upload-dit path :device)  cuda-dit.lisp:52
+    dit_velocity(d, context, p, latent, h, w, sigma,
+                 prefix_key=None, ref=None)           (dit-velocity ...)         cuda-dit.lisp:137
+    dit_release(d)                                    (dit-release d)            cuda-dit.lisp:99
+    euler_steps(d, context, p, z, h, w, sigmas, ...)  generate's loop            generate.lisp:133-135
+
+Errors are raised as ``ExnError`` carrying the library's message (the
+reference signals Lisp errors, e.g. open-dit's list of bad tensors).
+Arrays are numpy float32; latents channel-major (64, H, W).  Nothing here
+computes: a missing library or device raises, there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("EXN_B200_LIB", os.path.join(HERE, "libexn_b200.so"))
+
+# src/generate.lisp:7-9
+TURBO_SIGMAS = (1.0, 0.978453, 0.95418, 0.926626, 0.89508, 0.845148, 0.704534, 0.414568, 0.0)
+
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+EXN_OK = 0
+CODES = {1: "EINVAL", 2: "ECUDA", 3: "ESHAPE", 4: "ENOWEIGHTS", 5: "EIO", 6: "ETIMEOUT", 7: "ENOMEM",
+         8: "EUNSUPPORTED"}
+
+
+class ExnError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__("%s: %s" % (CODES.get(code, code), message))
+        self.code = code
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("width", ctypes.c_int), ("layers", ctypes.c_int), ("ffn", ctypes.c_int), ("latent", ctypes.c_int),
+                ("context", ctypes.c_int), ("freq", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("device", ctypes.c_int)]
+
+
+class Ref(ctypes.Structure):
+    _fields_ = [("a", ctypes.c_int), ("latent", ctypes.POINTER(ctypes.c_float)), ("rh", ctypes.c_int),
+                ("rw", ctypes.c_int)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded libexn_b200.so (raises if it is not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ExnError(8, "%s is not built (python ex-nihilo_b200/build.py)" % LIB_PATH)
+    L = ctypes.CDLL(LIB_PATH)
+    H = ctypes.c_void_p
+    fp = ctypes.POINTER(ctypes.c_float)
+    vp = ctypes.c_void_p
+    sigs = {
+        "exn_abi_version": (ctypes.c_int, []),
+        "exn_default_config": (None, [ctypes.POINTER(Config)]),
+        "exn_open": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.POINTER(H)]),
+        "exn_close": (None, [H]),
+        "exn_last_error": (ctypes.c_char_p, [H]),
+        "exn_load_gguf": (ctypes.c_int, [H, ctypes.c_char_p]),
+        "exn_check_gguf": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+        "exn_load_tensor": (ctypes.c_int, [H, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+                                           ctypes.POINTER(ctypes.c_int64), vp, ctypes.c_size_t]),
+        "exn_load_synthetic": (ctypes.c_int, [H, ctypes.c_uint64]),
+        "exn_weights_ready": (ctypes.c_int, [H]),
+        "exn_velocity": (ctypes.c_int, [H, fp, ctypes.c_int, fp, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                        ctypes.c_uint64, ctypes.POINTER(Ref), fp]),
+        "exn_generate": (ctypes.c_int, [H, fp, ctypes.c_int, fp, ctypes.c_int, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_double), ctypes.c_int, ctypes.c_uint64,
+                                        ctypes.POINTER(Ref)]),
+        "exn_generate_batch": (ctypes.c_int, [H, ctypes.c_int, fp, ctypes.c_int, fp, ctypes.c_int, ctypes.c_int,
+                                              ctypes.POINTER(ctypes.c_double), ctypes.c_int]),
+        "exn_generate_device": (ctypes.c_int, [H, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int,
+                                               ctypes.POINTER(ctypes.c_double), ctypes.c_int, vp]),
+        "exn_sync": (ctypes.c_int, [H]),
+        "exn_release": (ctypes.c_int, [H]),
+        # testing entry points (include/exn_b200_testing.h)
+        "exn_test_gemm": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
+        "exn_test_ln_mod": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "exn_test_qkv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
+        "exn_test_trace": (ctypes.c_int, [H, vp, ctypes.c_size_t]),
+        "exn_test_weight_bf16": (ctypes.c_int, [H, ctypes.c_char_p, vp, ctypes.c_size_t]),
+        "exn_test_synth_normal": (ctypes.c_int, [H, vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
+                                                 ctypes.c_double]),
+        "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 3),
+        "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
+        "exn_test_launch_count": (ctypes.c_longlong, [H]),
+    }
+    for name, (res, args) in sigs.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def _fp(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _f32(a, shape=None):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    if shape is not None and a.size != int(np.prod(shape)):
+        raise ExnError(1, "array of %d floats, expected %s" % (a.size, shape))
+    return a
+
+
+def prefix_key_of(key) -> int:
+    """A Lisp prefix key (any value compared with EQUAL: a prompt string, a
+    list) as the ABI's nonzero 64-bit key; None is NIL (0)."""
+    if key is None:
+        return 0
+    if isinstance(key, int) and 0 < key < 1 << 64:
+        return key
+    h = int.from_bytes(hashlib.blake2b(repr(key).encode(), digest_size=8).digest(), "little")
+    return h or 1
+
+
+def default_config(**kw) -> Config:
+    c = Config()
+    lib().exn_default_config(ctypes.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def check_gguf(path, **shape) -> None:
+    """open-dit (src/weights.lisp:47-61) without a device: raises ExnError
+    listing every problem."""
+    c = default_config(**shape)
+    buf = ctypes.create_string_buffer(8192)
+    rc = lib().exn_check_gguf(ctypes.byref(c), str(path).encode(), buf, len(buf))
+    if rc != EXN_OK:
+        raise ExnError(rc, buf.value.decode(errors="replace"))
+
+
+class Dit:
+    """A DiT on one CUDA device: the reference's GDIT structure."""
+
+    def __init__(self, device=0, **shape):
+        self.cfg = default_config(device=device, **shape)
+        h = ctypes.c_void_p()
+        rc = lib().exn_open(ctypes.byref(self.cfg), ctypes.byref(h))
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_last_error(None).decode(errors="replace"))
+        self.h = h
+
+    # -- plumbing
+    def _ck(self, rc):
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_last_error(self.h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().exn_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # -- weights
+    def load_gguf(self, path):
+        self._ck(lib().exn_load_gguf(self.h, str(path).encode()))
+
+    def load_tensor(self, name, ggml_type, dims, data: np.ndarray):
+        d = (ctypes.c_int64 * len(dims))(*dims)
+        data = np.ascontiguousarray(data)
+        self._ck(lib().exn_load_tensor(self.h, name.encode(), ggml_type, len(dims), d,
+                                       data.ctypes.data_as(ctypes.c_void_p), data.nbytes))
+
+    def load_synthetic(self, seed=1):
+        self._ck(lib().exn_load_synthetic(self.h, seed))
+
+    def ready(self) -> bool:
+        return lib().exn_weights_ready(self.h) == EXN_OK
+
+    # -- steps
+    def _ref(self, ref):
+        if ref is None:
+            return None, None
+        a, rlat, rh, rw = ref
+        rlat = _f32(rlat, (self.cfg.latent, rh, rw))
+        return Ref(a, _fp(rlat), rh, rw), rlat
+
+    def velocity(self, context, p, latent, h, w, sigma, prefix_key=None, ref=None):
+        ctx = _f32(context, (p, self.cfg.context))
+        lat = _f32(latent, (self.cfg.latent, h, w))
+        v = np.empty((self.cfg.latent, h, w), dtype=np.float32)
+        r, keep = self._ref(ref)
+        self._ck(lib().exn_velocity(self.h, _fp(ctx), p, _fp(lat), h, w, float(sigma), prefix_key_of(prefix_key),
+                                    ctypes.byref(r) if r is not None else None, _fp(v)))
+        del keep
+        return v
+
+    def generate(self, context, p, z, h, w, sigmas=TURBO_SIGMAS, prefix_key=None, ref=None):
+        ctx = _f32(context, (p, self.cfg.context))
+        zz = np.array(_f32(z, (self.cfg.latent, h, w)), copy=True).reshape(self.cfg.latent, h, w)
+        s = (ctypes.c_double * len(sigmas))(*sigmas)
+        r, keep = self._ref(ref)
+        self._ck(lib().exn_generate(self.h, _fp(ctx), p, _fp(zz), h, w, s, len(sigmas), prefix_key_of(prefix_key),
+                                    ctypes.byref(r) if r is not None else None))
+        del keep
+        return zz
+
+    def generate_batch(self, contexts, p, z, h, w, sigmas=TURBO_SIGMAS):
+        b = int(np.asarray(z).shape[0])
+        ctx = _f32(contexts, (b, p, self.cfg.context))
+        zz = np.array(_f32(z, (b, self.cfg.latent, h, w)), copy=True).reshape(b, self.cfg.latent, h, w)
+        s = (ctypes.c_double * len(sigmas))(*sigmas)
+        self._ck(lib().exn_generate_batch(self.h, b, _fp(ctx), p, _fp(zz), h, w, s, len(sigmas)))
+        return zz
+
+    def generate_device(self, batch, d_contexts, p, d_z, h, w, sigmas=TURBO_SIGMAS, stream=None):
+        """Device pointers (ints) in, queued on STREAM (an int cudaStream_t or None)."""
+        s = (ctypes.c_double * len(sigmas))(*sigmas)
+        self._ck(lib().exn_generate_device(self.h, batch, ctypes.c_void_p(d_contexts), p, ctypes.c_void_p(d_z), h, w,
+                                           s, len(sigmas), ctypes.c_void_p(stream) if stream else None))
+
+    def sync(self):
+        self._ck(lib().exn_sync(self.h))
+
+    def release(self):
+        self._ck(lib().exn_release(self.h))
+
+    def profile(self, on=True):
+        self._ck(lib().exn_test_profile(self.h, 1 if on else 0))
+
+    def last_profile(self):
+        g, a, o = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        self._ck(lib().exn_test_last_profile(self.h, ctypes.byref(g), ctypes.byref(a), ctypes.byref(o)))
+        return dict(gemm_ms=g.value, attn_ms=a.value, other_ms=o.value)
+
+    def launch_count(self):
+        return int(lib().exn_test_launch_count(self.h))
+
+
+# ---- the reference's names
+
+def upload_dit(path, device=0, **shape) -> Dit:
+    """(upload-dit path :device device), src/cuda-dit.lisp:52-86."""
+    d = Dit(device=device, **shape)
+    try:
+        d.load_gguf(path)
+    except Exception:
+        d.close()
+        raise
+    return d
+
+
+def dit_velocity(d: Dit, context, p, latent, h, w, sigma, prefix_key=None, ref=None):
+    """(dit-velocity d context p latent h w sigma :prefix-key :ref), src/cuda-dit.lisp:137-243."""
+    return d.velocity(context, p, latent, h, w, sigma, prefix_key=prefix_key, ref=ref)
+
+
+def dit_release(d: Dit):
+    """(dit-release d), src/cuda-dit.lisp:99-108."""
+    d.release()
+
+
+def euler_steps(d: Dit, context, p, z, h, w, sigmas=TURBO_SIGMAS, prefix_key=None, ref=None):
+    """generate's loop (src/generate.lisp:133-135) with the update fused on the device."""
+    return d.generate(context, p, z, h, w, sigmas, prefix_key=prefix_key, ref=ref)

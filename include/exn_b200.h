@@ -1,0 +1,143 @@
+/* exn_b200.h -- C ABI of libexn_b200.so, the B200 (sm_100a) DiT of
+ * Qwen-Image-2.1-Turbo behind ex-nihilo's calling conventions.
+ *
+ * Each entry point replaces one function of ex-nihilo's CUDA driver
+ * (paths relative to that project):
+ *
+ *   exn_load_gguf      (upload-dit path :device d)        src/cuda-dit.lisp:52-86
+ *                      with open-dit's checks              src/weights.lisp:47-61
+ *   exn_velocity       (dit-velocity d context p latent h w sigma
+ *                                    :prefix-key :ref)   src/cuda-dit.lisp:137-243
+ *   exn_release        (dit-release d)                    src/cuda-dit.lisp:99-108
+ *   exn_generate       the step loop of generate / edit   src/generate.lisp:133-135, 95-97
+ *                      (z += (s' - s) v, each v a dit-velocity call)
+ *   exn_generate_batch / exn_generate_device
+ *                      the same loop for B independent pictures (no counterpart:
+ *                      the reference runs one picture at a time)
+ *
+ * Conventions: every function returns an int status (EXN_OK = 0); the text
+ * of the last failure is exn_last_error(h).  Nothing aborts or throws across
+ * the ABI.  Host pointers belong to the caller, are read or written only
+ * during the call and need not be pinned.  A handle owns one CUDA device
+ * and is used by one thread at a time (the reference serialises callers with
+ * *gpu-lock*, src/server.lisp:24-28).  Floats are IEEE binary32; latents are
+ * channel-major 64 x H x W as in the reference.
+ */
+#ifndef EXN_B200_H
+#define EXN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXN_ABI_VERSION 1
+
+enum {
+  EXN_OK = 0,
+  EXN_EINVAL = 1,      /* bad argument: null pointer, size, shape */
+  EXN_ECUDA = 2,       /* a CUDA call failed */
+  EXN_ESHAPE = 3,      /* weights that are not the DiT's (open-dit's error) */
+  EXN_ENOWEIGHTS = 4,  /* a step before every tensor was loaded */
+  EXN_EIO = 5,         /* file could not be read */
+  EXN_ETIMEOUT = 6,    /* a kernel gave up waiting on its own pipeline */
+  EXN_ENOMEM = 7,      /* device memory exhausted */
+  EXN_EUNSUPPORTED = 8 /* no sm_100 device, or a tensor type not handled */
+};
+
+/* ggml tensor types accepted by exn_load_tensor */
+enum { EXN_GGML_F32 = 0, EXN_GGML_F16 = 1, EXN_GGML_Q8_0 = 8, EXN_GGML_BF16 = 30 };
+
+/* The model's shape: dit-shape of src/weights.lisp:19-20.  width must be a
+ * multiple of 256 and of head_dim (128), ffn of 128, context of 64. */
+typedef struct exn_config {
+  int width;    /* 4096 */
+  int layers;   /* 32 */
+  int ffn;      /* 12288 */
+  int latent;   /* 64 */
+  int context;  /* 4096: the encoder's state width */
+  int freq;     /* 256: timestep embedding size */
+  int head_dim; /* 128 */
+  int device;   /* CUDA ordinal */
+} exn_config;
+
+/* An edit's reference picture, the REF argument of dit-velocity
+ * (src/cuda-dit.lisp:142-147): its latent (64 x rh x rw, channel-major,
+ * normalised) goes into the prefix after the first A text rows. */
+typedef struct exn_ref {
+  int a;
+  const float* latent;
+  int rh, rw;
+} exn_ref;
+
+typedef struct exn_handle exn_handle;
+
+int exn_abi_version(void);
+void exn_default_config(exn_config* cfg);
+
+/* Open the device cfg->device.  *out is NULL on failure; the message is then
+ * exn_last_error(NULL) (per thread). */
+int exn_open(const exn_config* cfg, exn_handle** out);
+void exn_close(exn_handle* h);
+const char* exn_last_error(const exn_handle* h);
+
+/* upload-dit: read, check (architecture qwen_image, every tensor's name and
+ * dims, nothing extra; src/weights.lisp:47-61) and upload a DiT GGUF. */
+int exn_load_gguf(exn_handle* h, const char* path);
+
+/* open-dit alone: check the GGUF at PATH against the shape CFG (architecture,
+ * names, dims, no extra tensors) without a device.  EXN_OK, or EXN_ESHAPE /
+ * EXN_EIO with open-dit's message (one line per problem) copied into MSG. */
+int exn_check_gguf(const exn_config* cfg, const char* path, char* msg, size_t msg_len);
+
+/* One tensor from host memory, in its GGUF encoding: name without the
+ * "model.diffusion_model." prefix, ggml dims (contiguous axis first). */
+int exn_load_tensor(exn_handle* h, const char* name, int ggml_type, int n_dims, const int64_t* dims,
+                    const void* data, size_t nbytes);
+
+/* Every tensor from the deterministic synthetic generator (Q8_0 matrices,
+ * N(0, 0.02 sqrt(4096/width)) before quantisation; norms 1 + N(0, .)), the
+ * same bits as the test oracle's generator for SEED. */
+int exn_load_synthetic(exn_handle* h, uint64_t seed);
+
+/* EXN_OK when every tensor of the shape has been loaded. */
+int exn_weights_ready(const exn_handle* h);
+
+/* dit-velocity: v (64 x h x w) at noise level SIGMA.  CONTEXT is P x context
+ * floats (text rows only; with REF the picture's rows are added).  With a
+ * nonzero PREFIX_KEY the prompt's keys and values are kept after the call
+ * and reused by the next call with the same key and prefix length. */
+int exn_velocity(exn_handle* h, const float* context, int p, const float* latent, int hh, int ww, double sigma,
+                 uint64_t prefix_key, const exn_ref* ref, float* v_out);
+
+/* The Euler loop of generate/edit: for each pair (s, s') of SIGMAS,
+ * z += (s' - s) * dit-velocity(z, s), z (64 x h x w) updated in place on
+ * the device and copied back once.  PREFIX_KEY as exn_velocity. */
+int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, int ww, const double* sigmas,
+                 int nsig, uint64_t prefix_key, const exn_ref* ref);
+
+/* The same loop for BATCH independent pictures of the same size and prompt
+ * length: contexts B x P x context, z B x 64 x h x w (host memory).  The
+ * prompt K/V cache lives for the call only. */
+int exn_generate_batch(exn_handle* h, int batch, const float* contexts, int p, float* z, int hh, int ww,
+                       const double* sigmas, int nsig);
+
+/* exn_generate_batch on device memory (d_contexts, d_z are CUDA device
+ * pointers of the handle's device), ordered on STREAM (a cudaStream_t; NULL:
+ * the handle's own stream).  Returns once the work is queued. */
+int exn_generate_device(exn_handle* h, int batch, const float* d_contexts, int p, float* d_z, int hh, int ww,
+                        const double* sigmas, int nsig, void* stream);
+
+/* Wait for the handle's queued work and report any kernel failure. */
+int exn_sync(exn_handle* h);
+
+/* dit-release: free the step buffers and the kept prompt keys and values. */
+int exn_release(exn_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXN_B200_H */

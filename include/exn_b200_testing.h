@@ -1,0 +1,65 @@
+/* exn_b200_testing.h -- entry points for kernel-level parity tests and
+ * benchmarks.  They expose single kernels of libexn_b200.so on device
+ * pointers; none of them has a counterpart in ex-nihilo, whose kernels are
+ * reached only through dit-velocity (src/cuda-dit.lisp:137-243).  The
+ * reference's own kernel tests (inspect/metal-kernels-test.lisp:91-146) check
+ * LayerNorm-mod, QK-norm + RoPE and the attention mask; these entry points
+ * let the same cases run against the sm_100a kernels. */
+#ifndef EXN_B200_TESTING_H
+#define EXN_B200_TESTING_H
+
+#include "exn_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* C[M x N] (f32, row stride N) = A[M x K] (bf16) . B[N x K]^T (bf16) through
+ * the tcgen05 GEMM; all device pointers. */
+int exn_test_gemm(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k);
+
+/* Masked attention (xa_lim, src/cuda/dit.cu:60-66) on bf16 device tensors:
+ * q [batch][nq][heads*128], k/v [batch][kv_rows][heads*128], out like q. */
+int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
+                       int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
+
+/* LayerNorm(x) * (1 + mod[row kind]) -> bf16 (x_ln_mod, src/cuda/dit.cu:17-32):
+ * rows n, mod [2][width] (row 1 for prompt rows, n0 + t < p). */
+int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, int n, int width, int n0, int p);
+
+/* The fused QKV epilogue alone: y [n][width] bf16, the handle's layer LAYER
+ * weights; q out [n][width], k/v out [kv_rows][width] at rows n0.., bf16;
+ * RoPE of the plain layout (p text rows, hh x ww picture). */
+int exn_test_qkv(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p, int hh,
+                 int ww, int kv_rows);
+
+/* The residual stream x after every block (and txt_in's output first) of
+ * the next exn_velocity call, copied into HOST (layers + 1 blocks of
+ * rows x width floats, rows = the rows that call computes).  NULL disables. */
+int exn_test_trace(exn_handle* h, float* host, size_t floats);
+
+/* A Q8_0 tensor as the handle holds it (GEMV matrices only), or the bf16
+ * copy of a GEMM matrix: for comparing exn_load_synthetic with the oracle. */
+int exn_test_weight_bf16(exn_handle* h, const char* name, void* host_bf16, size_t elems);
+
+/* N floats offset * scale from the synthetic generator (stream, seed) into
+ * device memory: the oracle's synth_normal. */
+int exn_test_synth_normal(exn_handle* h, float* d, int64_t n, uint64_t seed, uint32_t stream, double std);
+
+/* Turn per-category kernel timing on or off (also on when EXN_PROFILE is set
+ * at open): CUDA events recorded on the handle's stream between the GEMM,
+ * attention and other kernels of every step. */
+int exn_test_profile(exn_handle* h, int on);
+
+/* Kernels of this library the handle has queued since it was opened. */
+long long exn_test_launch_count(const exn_handle* h);
+
+/* Kernel time of the last exn_generate* / exn_velocity call in ms per
+ * category (gemm, attention, other) when timing is on, else zeros. */
+int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,146 @@
+"""Single sm_100a kernels through the C ABI's testing entry points
+(include/exn_b200_testing.h), on the cases of the reference's own kernel
+tests (inspect/metal-kernels-test.lisp:91-146) and larger ones."""
+import numpy as np
+import pytest
+
+import exn_b200 as E
+from oracle import dit_oracle as O
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+TINY = dict(width=256, layers=2, ffn=768, context=256)
+
+
+@pytest.fixture(scope="module")
+def dit():
+    d = E.Dit(**TINY)
+    d.load_synthetic(1)
+    yield d
+    d.close()
+
+
+def bf16(a):
+    return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 64, 64), (100, 256, 256), (128, 256, 4096), (300, 512, 192),
+                                   (1000, 768, 1024), (4224, 12288, 4096), (513, 64, 4096)])
+def test_gemm_matches_fp64(dit, m, n, k):
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+    ad, bd = a.cuda(), b.cuda()
+    c = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    dit._ck(E.lib().exn_test_gemm(dit.h, ad.data_ptr(), bd.data_ptr(), c.data_ptr(), m, n, k))
+    ref = (ad.double() @ bd.double().T)
+    err = (c.double() - ref).abs().max().item() / ref.abs().max().item()
+    assert torch.isfinite(c).all()
+    assert err < 1e-5, err
+
+
+def attention_ref(q, k, v, q0, p, l, b0, b1, heads):
+    """fp64 masked softmax attention on the (already bf16-rounded) inputs."""
+    qq = q.double().reshape(q.shape[0], heads, 128)
+    kk = k[:l].double().reshape(l, heads, 128)
+    vv = v[:l].double().reshape(l, heads, 128)
+    lim = torch.as_tensor(O.xa_lim(np.arange(q0, q0 + q.shape[0]), p, l, b0, b1))
+    mask = torch.arange(l)[None, :] > lim[:, None]
+    s = torch.einsum("qhd,khd->hqk", qq, kk) / np.sqrt(128.0)
+    s = s.masked_fill(mask[None], float("-inf"))
+    return torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(q.shape[0], heads * 128)
+
+
+# (name, batch, nq, q0, p, l, b0, b1, heads): the first three are metal-kernels-test.lisp:144-146
+CASES = [
+    ("first pass: prompt causal, image all", 1, 77, 0, 20, 77, 20, 20, 32),
+    ("image after a cached prompt", 1, 70, 33, 33, 103, 33, 33, 32),
+    ("reference picture in the prompt", 1, 90, 0, 40, 90, 12, 30, 32),
+    ("two samples, tile tails", 2, 300, 0, 40, 300, 0, 0, 4),
+    ("cached, several key tiles", 2, 513, 128, 128, 641, 0, 0, 2),
+    ("1024^2 first step, 2 heads", 1, 4224, 0, 128, 4224, 0, 0, 2),
+    ("edit layout", 1, 700, 0, 300, 700, 8, 264, 2),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_attention_mask_cases(dit, case):
+    _, batch, nq, q0, p, l, b0, b1, heads = case
+    w = heads * 128
+    kv_rows = l + 5
+    g = torch.Generator().manual_seed(nq + l)
+    q = ((torch.rand(batch, nq, w, generator=g) * 4 - 2)).to(torch.bfloat16)
+    k = ((torch.rand(batch, kv_rows, w, generator=g) * 4 - 2)).to(torch.bfloat16)
+    v = ((torch.rand(batch, kv_rows, w, generator=g) * 2 - 1)).to(torch.bfloat16)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    out = torch.full((batch, nq, w), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dit._ck(E.lib().exn_test_attention(dit.h, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(),
+                                       batch, nq, q0, p, l, b0, b1, heads, kv_rows))
+    got = out.float().cpu()
+    for b in range(batch):
+        want = attention_ref(q[b], k[b], v[b], q0, p, l, b0, b1, heads)
+        err = (got[b].double() - want).abs().max().item()
+        # the reference's bound for half P (metal-kernels-test.lisp:5-8); bf16 P rounds at 2^-9 and
+        # the output itself is bf16 (|v| < 1)
+        assert err < 3e-3 + 2 ** -8, (b, err)
+
+
+def test_ln_mod_row_selection(dit):
+    # metal-kernels-test.lisp:91-102: rows n0 + t < p take the second modulation row
+    wd, n, n0, p = 4096, 9, 3, 6
+    rs = np.random.default_rng(7)
+    x = (rs.uniform(-1, 1, (n, wd)) * 50).astype(np.float32)
+    mod = rs.uniform(-1, 1, (2, wd)).astype(np.float32)
+    xd, md = torch.from_numpy(x).cuda(), torch.from_numpy(mod).cuda()
+    y = torch.empty(n, wd, dtype=torch.bfloat16, device="cuda")
+    dit._ck(E.lib().exn_test_ln_mod(dit.h, xd.data_ptr(), y.data_ptr(), md.data_ptr(), n, wd, n0, p))
+    xx = x.astype(np.float64)
+    m = xx.mean(1, keepdims=True)
+    inv = 1 / np.sqrt(((xx - m) ** 2).mean(1, keepdims=True) + 1e-6)
+    row = np.where(n0 + np.arange(n) < p, 1, 0)
+    want = (xx - m) * inv * (1 + mod[row].astype(np.float64))
+    got = y.float().cpu().numpy()
+    maxrel = np.abs(got - want).max() / np.abs(want).max()
+    assert maxrel < 2 ** -8, maxrel   # bf16 output (it feeds a bf16 GEMM)
+    exact = (got == torch.from_numpy(want).to(torch.bfloat16).float().numpy()).mean()
+    assert exact > 0.99, exact
+
+
+def test_synthetic_weights_match_the_oracle(dit):
+    sw = O.SynthWeights.make(O.Shape(**TINY), seed=1)
+    for name, dims in O.expected_tensors(O.Shape(**TINY)):
+        if len(dims) != 2:
+            continue
+        want = bf16(sw(name)).view(torch.int16).numpy()
+        got = np.empty(want.shape, dtype=np.int16)
+        dit._ck(E.lib().exn_test_weight_bf16(dit.h, name.encode(), got.ctypes.data, got.size))
+        assert np.array_equal(got, want), name
+
+
+def test_qkv_epilogue_norm_rope(dit):
+    # the fused to_q/to_k/to_v GEMM epilogue against ref_dit.py:135-139's arithmetic
+    sh = O.Shape(**TINY)
+    sw = O.SynthWeights.make(sh, seed=1)
+    p, hh, ww = 5, 3, 4
+    n0, n = 0, p + hh * ww
+    rs = np.random.default_rng(3)
+    y = bf16(rs.standard_normal((n, sh.width)))
+    yd = y.cuda()
+    q = torch.empty(n, sh.width, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(n + 3, sh.width, dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros(n + 3, sh.width, dtype=torch.bfloat16, device="cuda")
+    dit._ck(E.lib().exn_test_qkv(dit.h, 1, yd.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), n, n0, p, hh, ww,
+                                 n + 3))
+    b = "transformer_blocks.1."
+    yy = y.double().numpy()
+    cos, sin = O.rope_tables(O.dit_positions(p, hh, ww))
+    heads = sh.heads
+    for name, out, norm in [("to_q", q, "norm_q"), ("to_k", k[:n], "norm_k"), ("to_v", v[:n], None)]:
+        wq = bf16(sw(b + "attn." + name + ".weight")).double().numpy()
+        want = (yy @ wq.T).reshape(n, heads, 128)
+        if norm:
+            want = O.rope(O.rmsnorm(want, sw.vec[b + "attn." + norm + ".weight"].astype(np.float64)), cos, sin)
+        want = want.reshape(n, sh.width)
+        got = out.float().cpu().numpy()
+        maxrel = np.abs(got - want).max() / np.abs(want).max()
+        assert maxrel < 2 ** -7, (name, maxrel)
