@@ -34,8 +34,12 @@ constexpr int ATT_THREADS = 320;
 constexpr int TILE = 128;                 // queries per tile, keys per K/V tile
 constexpr int HALF = TILE * 128;          // bytes of one 64-column swizzled half of a 128 x 128 bf16 tile
 constexpr int TILE_BYTES = 2 * HALF;      // 32 KB
-constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_K = 2 * TILE_BYTES, OFF_V = 3 * TILE_BYTES;
-constexpr int OFF_PA = 4 * TILE_BYTES, OFF_PB = 5 * TILE_BYTES, OFF_BAR = 6 * TILE_BYTES;
+// K_0 V_0 K_1 V_1 ... stream through a ring of 3 tile slots, so each load has
+// a slot free well before its MMA needs it (K_{j+1} reuses V_{j-1}'s slot,
+// V_{j+1} reuses K_j's).
+constexpr int SLOTS = 3;
+constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_SLOT = 2 * TILE_BYTES;
+constexpr int OFF_PA = (2 + SLOTS) * TILE_BYTES, OFF_PB = (3 + SLOTS) * TILE_BYTES, OFF_BAR = (4 + SLOTS) * TILE_BYTES;
 constexpr int ATT_SMEM = OFF_BAR + 256 + 1024;
 constexpr uint32_t IDESC_S = idesc_bf16(128, 128);
 constexpr uint32_t IDESC_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (dims contiguous)
@@ -46,7 +50,7 @@ __device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
 }
 
 struct Bars {
-  uint64_t q_full, k_full, k_empty, v_full, v_empty;
+  uint64_t q_full, slot_full[SLOTS], slot_empty[SLOTS];
   uint64_t s_full[2], p_full[2], o_full[2];
   uint64_t done;
   uint32_t tmem_slot;
@@ -72,10 +76,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->k_full, 1);
-    mbar_init(&bars->k_empty, 1);
-    mbar_init(&bars->v_full, 1);
-    mbar_init(&bars->v_empty, 1);
+    for (int i = 0; i < SLOTS; ++i) {
+      mbar_init(&bars->slot_full[i], 1);
+      mbar_init(&bars->slot_empty[i], 1);
+    }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->s_full[x], 1);
       mbar_init(&bars->p_full[x], 4);
@@ -106,81 +110,86 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int hf = 0; hf < 2; ++hf)
           tma_load_3d(smem + (x ? OFF_QB : OFF_QA) + hf * HALF, &tmQ, &bars->q_full, hx + hf * 64,
                       qt * 2 * TILE + x * TILE, sample);
-      int k_issued = -1, v_issued = -1;
-      for (int j = 0; j < nkv; ++j) {
-        const uint32_t par = (j & 1) ^ 1;
-        if (!mbar_wait(&bars->k_empty, par, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&bars->k_full, TILE_BYTES);
+      // load number t: K_{t/2} for even t, V_{t/2} for odd t; slot t % 3, its (t / 3)-th use
+      int issued = 0;
+      for (int t = 0; t < 2 * nkv; ++t) {
+        const int slot = t % SLOTS;
+        const uint32_t use = static_cast<uint32_t>(t / SLOTS);
+        if (!mbar_wait(&bars->slot_empty[slot], (use & 1) ^ 1, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&bars->slot_full[slot], TILE_BYTES);
+        const CUtensorMap* map = (t & 1) ? &tmV : &tmK;
         for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem + OFF_K + hf * HALF, &tmK, &bars->k_full, hx + hf * 64, j * TILE, sample);
-        k_issued = j;
-        if (!mbar_wait(&bars->v_empty, par, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&bars->v_full, TILE_BYTES);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem + OFF_V + hf * HALF, &tmV, &bars->v_full, hx + hf * 64, j * TILE, sample);
-        v_issued = j;
+          tma_load_3d(smem + OFF_SLOT + slot * TILE_BYTES + hf * HALF, map, &bars->slot_full[slot], hx + hf * 64,
+                      (t >> 1) * TILE, sample);
+        issued = t + 1;
       }
       if (*abort_flag) {  // the copies in flight land before the CTA leaves
         volatile int no_abort = 0;
         mbar_wait(&bars->q_full, 0, &no_abort, nullptr, 0);
-        if (k_issued >= 0) mbar_wait(&bars->k_full, k_issued & 1, &no_abort, nullptr, 0);
-        if (v_issued >= 0) mbar_wait(&bars->v_full, v_issued & 1, &no_abort, nullptr, 0);
+        for (int t = issued - SLOTS < 0 ? 0 : issued - SLOTS; t < issued; ++t)
+          mbar_wait(&bars->slot_full[t % SLOTS], static_cast<uint32_t>(t / SLOTS) & 1, &no_abort, nullptr, 0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t qa = smem_u32(smem + OFF_QA), qb = smem_u32(smem + OFF_QB);
-      const uint32_t kk_base = smem_u32(smem + OFF_K), v_base = smem_u32(smem + OFF_V);
+      const uint32_t slot0 = smem_u32(smem + OFF_SLOT);
       const uint32_t pa = smem_u32(smem + OFF_PA), pb = smem_u32(smem + OFF_PB);
-      auto issue_s = [&](uint32_t q_addr, uint32_t d) {
+      auto issue_s = [&](uint32_t q_addr, uint32_t k_addr, uint32_t d) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t o = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(d, sdesc_sw128(q_addr + o, 16, 1024), sdesc_sw128(kk_base + o, 16, 1024), IDESC_S,
-                  kk ? 1u : 0u);
+          umma_ss(d, sdesc_sw128(q_addr + o, 16, 1024), sdesc_sw128(k_addr + o, 16, 1024), IDESC_S, kk ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t p_addr, uint32_t d, bool acc) {
+      auto issue_pv = [&](uint32_t p_addr, uint32_t v_addr, uint32_t d, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_base + kk * 2048, HALF, 1024);
+          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, HALF, 1024);
           umma_ss(d, ad, bd, IDESC_PV, (acc || kk) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) &&
-                mbar_wait(&bars->k_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN);
+      // wait for load T (K_{T/2} or V_{T/2}); its slot's address
+      auto wait_load = [&](int t, uint32_t& addr) -> bool {
+        const int slot = t % SLOTS;
+        addr = slot0 + slot * TILE_BYTES;
+        return mbar_wait(&bars->slot_full[slot], static_cast<uint32_t>(t / SLOTS) & 1, abort_flag, status,
+                         STATUS_TIMEOUT_ATTN);
+      };
+      uint32_t k_addr = 0, v_addr = 0;
+      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) && wait_load(0, k_addr);
       if (ok) {
         tc_fence_after();
-        issue_s(qa, tmem + 0);
+        issue_s(qa, k_addr, tmem + 0);
         umma_commit(&bars->s_full[0]);
-        issue_s(qb, tmem + 128);
+        issue_s(qb, k_addr, tmem + 128);
         umma_commit(&bars->s_full[1]);
-        umma_commit(&bars->k_empty);
+        umma_commit(&bars->slot_empty[0]);
       }
       for (int j = 0; j < nkv && ok; ++j) {
         const uint32_t par = j & 1;
         const bool more = j + 1 < nkv;
-        if (!(ok = mbar_wait(&bars->v_full, par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+        if (!(ok = wait_load(2 * j + 1, v_addr))) break;
         if (!(ok = mbar_wait(&bars->p_full[0], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(pa, tmem + 256, j > 0);
+        issue_pv(pa, v_addr, tmem + 256, j > 0);
         if (!more) umma_commit(&bars->o_full[0]);
         if (more) {
-          if (!(ok = mbar_wait(&bars->k_full, par ^ 1, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
+          if (!(ok = wait_load(2 * j + 2, k_addr))) break;
           tc_fence_after();
-          issue_s(qa, tmem + 0);
+          issue_s(qa, k_addr, tmem + 0);
           umma_commit(&bars->s_full[0]);
         }
         if (!(ok = mbar_wait(&bars->p_full[1], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(pb, tmem + 384, j > 0);
-        umma_commit(&bars->v_empty);
+        issue_pv(pb, v_addr, tmem + 384, j > 0);
+        umma_commit(&bars->slot_empty[(2 * j + 1) % SLOTS]);
         if (!more) umma_commit(&bars->o_full[1]);
         if (more) {
-          issue_s(qb, tmem + 128);
+          issue_s(qb, k_addr, tmem + 128);
           umma_commit(&bars->s_full[1]);
-          umma_commit(&bars->k_empty);
+          umma_commit(&bars->slot_empty[(2 * j + 2) % SLOTS]);
         }
       }
       umma_commit(&bars->done);
@@ -207,12 +216,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       tc_fence_after();
       float s[128];
+      {
+        uint32_t rr[128];
+        tmem_ld128(s_addr, rr);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(s_addr + c * 32, rr);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(rr[i]);
+        for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(rr[i]);
       }
       const int key0 = j * TILE;
       if (key0 + TILE - 1 > lim) {
@@ -220,9 +228,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int c = 0; c < 128; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // row maximum as an 8-way tree (a serial chain of 128 would cost its latency every tile)
+      float m8[8];
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < 128; c += 8)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = m_new > m + RESCALE_THRESHOLD;
       float alpha = 1.f;
@@ -242,21 +257,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         tmem_st_wait();
       }
-      float ps = 0.f;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c16 = 0; c16 < 16; ++c16) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           e[i] = fast_exp2(fmaf(s[c16 * 8 + i], scale_log2, -m));
-          ps += e[i];
+          ps8[i] += e[i];
         }
         const int half = c16 >> 3, cw = c16 & 7;
         *reinterpret_cast<uint4*>(prow + half * HALF + ((cw ^ (r & 7)) << 4)) =
             make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
                        pack_bf16x2(e[6], e[7]));
       }
-      lsum += ps;
+      lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

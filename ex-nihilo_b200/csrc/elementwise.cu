@@ -185,70 +185,78 @@ __global__ void k_temb(float* emb, double t, int freq) {
 }
 
 constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_ROWS = 4;  // output rows per warp: x is staged once per block of 32 rows
 constexpr int GEMV_MAXM = 2;
 
-// y[m][o] = act(sum_k x[m][k] W[o][k]); one warp per output row, W read once.
+// y[m][o] = act(sum_k x[m][k] W[o][k]).  Each lane reads 16 contiguous
+// weight bytes (Q8_0: half a block, the block scale shared by a lane pair)
+// or 8 bf16 / 4+4 f32, so a warp streams 512 (256) weights of a row per step.
 template <int KIND>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
     k_gemv(const void* __restrict__ wv, const __half* __restrict__ wd, const float* __restrict__ x,
            float* __restrict__ y, int m, int in, int out, int act, int piece) {
-  extern __shared__ float xs[];
-  for (int i = threadIdx.x; i < m * in; i += blockDim.x) xs[i] = x[i];
+  extern __shared__ float4 xs4[];
+  const float* xs = reinterpret_cast<const float*>(xs4);
+  for (int i = threadIdx.x; i < m * in / 4; i += blockDim.x) xs4[i] = reinterpret_cast<const float4*>(x)[i];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int o = blockIdx.x * GEMV_WARPS + warp;
-  if (o >= out) return;
-  float acc[GEMV_MAXM] = {0.f, 0.f};
-  if constexpr (KIND == W_Q8) {
-    const int8_t* q = static_cast<const int8_t*>(wv) + static_cast<long long>(o) * in;
-    const __half* d = wd + static_cast<long long>(o) * (in / 32);
-    for (int blk = lane; blk < in / 32; blk += 32) {
-      const int4 q0 = __ldg(reinterpret_cast<const int4*>(q + blk * 32));
-      const int4 q1 = __ldg(reinterpret_cast<const int4*>(q + blk * 32) + 1);
-      const int qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-      const float sc = __half2float(d[blk]);
-      for (int mm = 0; mm < m; ++mm) {
-        const float* xr = xs + mm * in + blk * 32;
-        float s = 0.f;
+  for (int rr = 0; rr < GEMV_ROWS; ++rr) {
+    const int o = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS + rr;
+    if (o >= out) return;
+    float acc[GEMV_MAXM] = {0.f, 0.f};
+    if constexpr (KIND == W_Q8) {
+      const int8_t* q = static_cast<const int8_t*>(wv) + static_cast<long long>(o) * in;
+      const __half* d = wd + static_cast<long long>(o) * (in / 32);
+      for (int k0 = lane * 16; k0 < in; k0 += 512) {
+        const int4 qv = __ldg(reinterpret_cast<const int4*>(q + k0));
+        const float sc = __half2float(d[k0 >> 5]);
+        const int qw[4] = {qv.x, qv.y, qv.z, qv.w};
+        for (int mm = 0; mm < m; ++mm) {
+          const float4* xr = reinterpret_cast<const float4*>(xs + mm * in + k0);
+          float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int wv4 = qw[k];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) s += static_cast<float>(static_cast<int8_t>((wv4 >> (8 * e)) & 0xFF)) * xr[4 * k + e];
+          for (int k = 0; k < 4; ++k) {
+            const float4 xv = xr[k];
+            const int w4 = qw[k];
+            s += static_cast<float>(static_cast<int8_t>(w4 & 0xFF)) * xv.x;
+            s += static_cast<float>(static_cast<int8_t>((w4 >> 8) & 0xFF)) * xv.y;
+            s += static_cast<float>(static_cast<int8_t>((w4 >> 16) & 0xFF)) * xv.z;
+            s += static_cast<float>(static_cast<int8_t>(w4 >> 24)) * xv.w;
+          }
+          acc[mm] += sc * s;
         }
-        acc[mm] += sc * s;
+      }
+    } else {
+      for (int k0 = lane * 8; k0 < in; k0 += 256) {
+        float wf[8];
+        if constexpr (KIND == W_BF16) {
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(wv) + static_cast<long long>(o) * in + k0));
+          const bf16* bp = reinterpret_cast<const bf16*>(&u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) wf[e] = __bfloat162float(bp[e]);
+        } else {
+          const float4* fp = reinterpret_cast<const float4*>(static_cast<const float*>(wv) + static_cast<long long>(o) * in + k0);
+          const float4 a = __ldg(fp), b = __ldg(fp + 1);
+          wf[0] = a.x; wf[1] = a.y; wf[2] = a.z; wf[3] = a.w; wf[4] = b.x; wf[5] = b.y; wf[6] = b.z; wf[7] = b.w;
+        }
+        for (int mm = 0; mm < m; ++mm) {
+          float s = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s += wf[e] * xs[mm * in + k0 + e];
+          acc[mm] += s;
+        }
       }
     }
-  } else {
-    for (int k0 = lane * 8; k0 < in; k0 += 256) {
-      float wf[8];
-      if constexpr (KIND == W_BF16) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(wv) + static_cast<long long>(o) * in + k0));
-        const bf16* bp = reinterpret_cast<const bf16*>(&u);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wf[e] = __bfloat162float(bp[e]);
-      } else {
-        const float4* fp = reinterpret_cast<const float4*>(static_cast<const float*>(wv) + static_cast<long long>(o) * in + k0);
-        const float4 a = __ldg(fp), b = __ldg(fp + 1);
-        wf[0] = a.x; wf[1] = a.y; wf[2] = a.z; wf[3] = a.w; wf[4] = b.x; wf[5] = b.y; wf[6] = b.z; wf[7] = b.w;
+    for (int mm = 0; mm < m; ++mm) {
+      float v = warp_sum(acc[mm]);
+      if (lane == 0) {
+        if (act == 1) v = v / (1.f + expf(-v));
+        if (act == 2) {
+          const int pc = o / piece;
+          if (pc == 1 || pc == 3) v = tanhf(v);
+        }
+        y[static_cast<long long>(mm) * out + o] = v;
       }
-      for (int mm = 0; mm < m; ++mm) {
-        float s = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) s += wf[e] * xs[mm * in + k0 + e];
-        acc[mm] += s;
-      }
-    }
-  }
-  for (int mm = 0; mm < m; ++mm) {
-    float v = warp_sum(acc[mm]);
-    if (lane == 0) {
-      if (act == 1) v = v / (1.f + expf(-v));
-      if (act == 2) {
-        const int pc = o / piece;
-        if (pc == 1 || pc == 3) v = tanhf(v);
-      }
-      y[static_cast<long long>(mm) * out + o] = v;
     }
   }
 }
@@ -420,7 +428,7 @@ void temb_launch(float* emb, double sigma, int freq, cudaStream_t st) {
 
 void gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out, int act,
                  int piece, cudaStream_t st) {
-  const unsigned grid = blocks_for(out, GEMV_WARPS);
+  const unsigned grid = blocks_for(out, GEMV_WARPS * GEMV_ROWS);
   const size_t sm = static_cast<size_t>(m) * in * sizeof(float);
   if (kind == W_Q8)
     k_gemv<W_Q8><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece);

@@ -44,8 +44,10 @@ __device__ __forceinline__ long long map_row(const GemmEpi& e, int r) {
   return static_cast<long long>(b) * e.seg_out + e.off + t + (t >= e.split_at ? e.split_gap : 0);
 }
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-  constexpr int GM = 16;  // 16 row blocks share each weight tile while it sits in L2
+// Tiles run in groups of GM row blocks, all columns of a group before the
+// next: a weight tile is read from HBM once per group while the group's
+// activation rows stay in L2.
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int GM, int& mb, int& nb) {
   const int group = tile / (GM * num_n);
   const int first = group * GM;
   const int gm = min(GM, num_m - first);
@@ -197,7 +199,7 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
 template <int BN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-           const GemmEpi ep, int* status) {
+           int group_m, const GemmEpi ep, int* status) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
             ok = false;
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      tile_coords(tile, num_m, num_n, group_m, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
@@ -398,9 +400,14 @@ static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t
   const uint64_t sb[1] = {static_cast<uint64_t>(g.ldb) * 2};
   const uint32_t bb[2] = {BK, BN};
   if (make_tmap_bf16(&ta, g.a, 2, da, sa, ba) || make_tmap_bf16(&tb, g.b, 2, db, sb, bb)) return -4;
-  const int tiles = ((g.M + BM - 1) / BM) * (g.N / BN);
+  const int num_m = (g.M + BM - 1) / BM;
+  const int tiles = num_m * (g.N / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  k_gemm<BN, EPI><<<grid, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, g.ep, d_status);
+  // as many row blocks per group as keep ~48 MB of activations in L2
+  int group_m = static_cast<int>((48ll << 20) / (static_cast<long long>(BM) * g.K * 2));
+  group_m = group_m < 8 ? 8 : group_m;
+  group_m = group_m > num_m ? num_m : group_m;
+  k_gemm<BN, EPI><<<grid, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, group_m, g.ep, d_status);
   return static_cast<int>(cudaGetLastError());
 }
 
