@@ -68,6 +68,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to HINT_NS while
+// the phase is incomplete (it resumes as soon as the phase completes), so a
+// waiting producer does not take issue slots from the warps sharing its SMSP.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase of parity PARITY to complete.  False when the CTA gave
 // up: another role already aborted, or this wait ran past EXN_WAIT_NS (then
 // it raises the abort flag and ORs CODE into *status).
@@ -76,7 +91,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > EXN_WAIT_NS) {
       *abort_flag = 1;
@@ -94,6 +109,19 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, code) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   return ok != 0;
+}
+
+// One lane of a converged warp, chosen by the hardware (elect.sync).  Loops
+// that issue TMA copies and MMAs run on the whole warp so the addresses and
+// descriptors they compute stay warp-uniform; only the issue is single-lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, px;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ----------------------------------------------------------------------------- TMA
