@@ -20,6 +20,8 @@
 //               row maximum grows by more than 2^8
 // The MMA order PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) lets one tile's softmax
 // run while the tensor core serves the other.
+#include <stdlib.h>
+
 #include "exn_device.cuh"
 #include "exn_internal.h"
 
@@ -45,6 +47,21 @@ constexpr uint32_t IDESC_S = idesc_bf16(128, 128);
 constexpr uint32_t IDESC_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (dims contiguous)
 constexpr float RESCALE_THRESHOLD = 8.0f;                          // log2 units
 
+// 2^x on the FMA and integer pipes, for x <= 8: Cody-Waite split x = n + f,
+// n = round(x) by the 1.5 * 2^23 magic add, f in [-1/2, 1/2]; 2^f by a
+// degree-3 polynomial fitted to 2^f on that interval (Lawson-weighted least
+// squares, max relative error 7.5e-5, far under bf16's 2^-9 rounding of P);
+// 2^n added into the exponent field; below 2^-126 (masked keys) exactly 0.
+// The MUFU pipe gives 16 ex2 a clock per SM; computing a share of each row
+// here lets the FMA pipes carry part of the softmax's exponentials.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float t = __fadd_rn(xc, 12582912.f);
+  const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.f));
+  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.24261114f), f, 0.69326097f), f, 0.99992806f);
+  return x > -126.f ? __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23)) : 0.f;
+}
+
 __device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
   return g >= p ? l - 1 : (g >= b0 && g < b1 ? b1 - 1 : g);
 }
@@ -59,6 +76,7 @@ struct Bars {
 
 }  // namespace
 
+template <int POLY>  // of each 8 exponentials of a row, POLY are computed by exp2_fma
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
@@ -132,22 +150,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t qa = smem_u32(smem + OFF_QA), qb = smem_u32(smem + OFF_QB);
+      // descriptors formed once; start addresses then advance in 16-byte units
+      const uint64_t dq_a = sdesc_sw128(smem_u32(smem + OFF_QA), 16, 1024);
+      const uint64_t dq_b = sdesc_sw128(smem_u32(smem + OFF_QB), 16, 1024);
+      const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), 16, 1024);     // keys x dims, K-major
+      const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), HALF, 1024);   // keys x dims read MN-major
+      const uint64_t dp_a = sdesc_sw128(smem_u32(smem + OFF_PA), 16, 1024);
+      const uint64_t dp_b = sdesc_sw128(smem_u32(smem + OFF_PB), 16, 1024);
       const uint32_t slot0 = smem_u32(smem + OFF_SLOT);
-      const uint32_t pa = smem_u32(smem + OFF_PA), pb = smem_u32(smem + OFF_PB);
-      auto issue_s = [&](uint32_t q_addr, uint32_t k_addr, uint32_t d) {
+      auto issue_s = [&](uint64_t dq, uint32_t k_addr, uint32_t d) {
+        const uint64_t dk = dk0 + static_cast<uint64_t>((k_addr - slot0) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t o = (kk >> 2) * HALF + (kk & 3) * 32;
-          umma_ss(d, sdesc_sw128(q_addr + o, 16, 1024), sdesc_sw128(k_addr + o, 16, 1024), IDESC_S, kk ? 1u : 0u);
+          const uint64_t o = static_cast<uint64_t>(((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
+          umma_ss(d, dq + o, dk + o, IDESC_S, kk ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t p_addr, uint32_t v_addr, uint32_t d, bool acc) {
+      auto issue_pv = [&](uint64_t dp, uint32_t v_addr, uint32_t d, bool acc) {
+        const uint64_t dv = dv0 + static_cast<uint64_t>((v_addr - slot0) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, HALF, 1024);
-          umma_ss(d, ad, bd, IDESC_PV, (acc || kk) ? 1u : 0u);
+          const uint64_t o = static_cast<uint64_t>(((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
+          umma_ss(d, dp + o, dv + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV, (acc || kk) ? 1u : 0u);
         }
       };
       // wait for load T (K_{T/2} or V_{T/2}); its slot's address
@@ -161,9 +185,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) && wait_load(0, k_addr);
       if (ok) {
         tc_fence_after();
-        issue_s(qa, k_addr, tmem + 0);
+        issue_s(dq_a, k_addr, tmem + 0);
         umma_commit(&bars->s_full[0]);
-        issue_s(qb, k_addr, tmem + 128);
+        issue_s(dq_b, k_addr, tmem + 128);
         umma_commit(&bars->s_full[1]);
         umma_commit(&bars->slot_empty[0]);
       }
@@ -173,21 +197,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!(ok = wait_load(2 * j + 1, v_addr))) break;
         if (!(ok = mbar_wait(&bars->p_full[0], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(pa, v_addr, tmem + 256, j > 0);
+        issue_pv(dp_a, v_addr, tmem + 256, j > 0);
         if (!more) umma_commit(&bars->o_full[0]);
         if (more) {
           if (!(ok = wait_load(2 * j + 2, k_addr))) break;
           tc_fence_after();
-          issue_s(qa, k_addr, tmem + 0);
+          issue_s(dq_a, k_addr, tmem + 0);
           umma_commit(&bars->s_full[0]);
         }
         if (!(ok = mbar_wait(&bars->p_full[1], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(pb, v_addr, tmem + 384, j > 0);
+        issue_pv(dp_b, v_addr, tmem + 384, j > 0);
         umma_commit(&bars->slot_empty[(2 * j + 1) % SLOTS]);
         if (!more) umma_commit(&bars->o_full[1]);
         if (more) {
-          issue_s(qb, k_addr, tmem + 128);
+          issue_s(dq_b, k_addr, tmem + 128);
           umma_commit(&bars->s_full[1]);
           umma_commit(&bars->slot_empty[(2 * j + 2) % SLOTS]);
         }
@@ -263,7 +287,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = fast_exp2(fmaf(s[c16 * 8 + i], scale_log2, -m));
+          const float xv = fmaf(s[c16 * 8 + i], scale_log2, -m);
+          e[i] = i >= 8 - POLY ? exp2_fma(xv) : fast_exp2(xv);
           ps8[i] += e[i];
         }
         const int half = c16 >> 3, cw = c16 & 7;
@@ -309,11 +334,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   if (a.nq <= 0 || a.l <= 0 || a.width % 128 || a.heads * 128 != a.width || a.kv_rows < a.l) return -1;
   if (a.q0 + a.nq > a.l) return -1;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
+  static int poly = -1;  // EXN_ATTN_POLY: exponentials of each 8 on the FMA pipes (0, 1, 2 or 3)
+  if (poly < 0) {
+    const char* e = getenv("EXN_ATTN_POLY");
+    const int v = e ? atoi(e) : 0;
+    if (cudaFuncSetAttribute(k_attention<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attention<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attention<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attention<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
       return -3;
-    attr = true;
+    poly = v < 0 || v > 3 ? 0 : v;
   }
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, TILE, 1};
@@ -326,8 +356,9 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
   dim3 grid((a.nq + 2 * TILE - 1) / (2 * TILE), a.heads, a.batch);
-  k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
-                                                   a.scale_log2, d_status);
+  auto kern = poly == 0 ? k_attention<0> : poly == 1 ? k_attention<1> : poly == 2 ? k_attention<2> : k_attention<3>;
+  kern<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
+                                            a.scale_log2, d_status);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -284,6 +284,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
+      // descriptors formed once; start addresses then advance in 16-byte units
+      const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, 1024);
+      const uint64_t b_desc0 = sdesc_sw128(smem_u32(sB), 16, 1024);
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
@@ -296,14 +299,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+          const uint64_t ad = a_desc0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
+          const uint64_t bd = b_desc0 + static_cast<uint64_t>((stage * C::B_BYTES) >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_ss(d_tmem, ad, bd, C::IDESC, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k) umma_ss(d_tmem, ad + 2 * k, bd + 2 * k, C::IDESC, (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
