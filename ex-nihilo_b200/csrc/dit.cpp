@@ -1082,22 +1082,18 @@ int exn_generate_device(exn_handle* h, int batch, const float* d_contexts, int p
   if ((rc = use_device(h)) || (rc = check_step_args(h, batch, p, hh, ww, nullptr))) return rc;
   const int nimg = hh * ww;
   if ((rc = ensure_buffers(h, batch, p + nimg, p + nimg, p, nimg, 0))) return rc;
+  // ordered after the caller's stream (NULL is CUDA's default stream), and the caller's stream after the work
   cudaStream_t user = static_cast<cudaStream_t>(stream);
-  if (user) {  // order after the caller's stream, and the caller's stream after us
-    cudaEvent_t e;
-    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    CK(cudaEventRecord(e, user));
-    CK(cudaStreamWaitEvent(h->st, e, 0));
-    cudaEventDestroy(e);
-  }
+  cudaEvent_t e;
+  CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CK(cudaEventRecord(e, user));
+  CK(cudaStreamWaitEvent(h->st, e, 0));
+  cudaEventDestroy(e);
   if ((rc = generate_dev(h, batch, d_contexts, p, d_z, hh, ww, sigmas, nsig))) return rc;
-  if (user) {
-    cudaEvent_t e;
-    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    CK(cudaEventRecord(e, h->st));
-    CK(cudaStreamWaitEvent(user, e, 0));
-    cudaEventDestroy(e);
-  }
+  CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CK(cudaEventRecord(e, h->st));
+  CK(cudaStreamWaitEvent(user, e, 0));
+  cudaEventDestroy(e);
   return EXN_OK;
 }
 

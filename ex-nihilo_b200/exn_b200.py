@@ -236,11 +236,11 @@ class Dit:
         self._ck(lib().exn_generate_batch(self.h, b, _fp(ctx), p, _fp(zz), h, w, s, len(sigmas)))
         return zz
 
-    def generate_device(self, batch, d_contexts, p, d_z, h, w, sigmas=TURBO_SIGMAS, stream=None):
-        """Device pointers (ints) in, queued on STREAM (an int cudaStream_t or None)."""
+    def generate_device(self, batch, d_contexts, p, d_z, h, w, sigmas=TURBO_SIGMAS, stream=0):
+        """Device pointers (ints) in, ordered on STREAM (an int cudaStream_t; 0 is CUDA's default stream)."""
         s = (ctypes.c_double * len(sigmas))(*sigmas)
         self._ck(lib().exn_generate_device(self.h, batch, ctypes.c_void_p(d_contexts), p, ctypes.c_void_p(d_z), h, w,
-                                           s, len(sigmas), ctypes.c_void_p(stream) if stream else None))
+                                           s, len(sigmas), ctypes.c_void_p(stream or 0)))
 
     def sync(self):
         self._ck(lib().exn_sync(self.h))

@@ -125,8 +125,9 @@ int exn_generate_batch(exn_handle* h, int batch, const float* contexts, int p, f
                        const double* sigmas, int nsig);
 
 /* exn_generate_batch on device memory (d_contexts, d_z are CUDA device
- * pointers of the handle's device), ordered on STREAM (a cudaStream_t; NULL:
- * the handle's own stream).  Returns once the work is queued. */
+ * pointers of the handle's device), ordered on STREAM (a cudaStream_t; NULL
+ * is CUDA's default stream): the work starts after what STREAM already holds
+ * and what is queued on STREAM later waits for it.  Returns once queued. */
 int exn_generate_device(exn_handle* h, int batch, const float* d_contexts, int p, float* d_z, int hh, int ww,
                         const double* sigmas, int nsig, void* stream);
 
