@@ -188,6 +188,12 @@ def cpu_threads():
         return os.cpu_count()
 
 
+def all_host_threads():
+    """Every host core for the CPU legs (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    import threadpoolctl
+    return threadpoolctl.threadpool_limits(limits=os.cpu_count())
+
+
 # --------------------------------------------------------------------------- arms
 
 def init_dist(n):
@@ -356,9 +362,11 @@ def run_exn(args):
     if args.layers != LAYERS:
         out["config"]["workload"] += " -- PROFILING CASE with %d of 32 blocks, not a bench number" % args.layers
     if world == 1 and not args.no_cpu:
-        bs = cpu_block_seconds()
+        with all_host_threads():
+            bs = cpu_block_seconds()
+            threads = cpu_threads()
         out["cpu_baseline"] = {"value": round(1.0 / cpu_picture_seconds(bs), 6), "unit": "images/s",
-                               "cores": cpu_threads(), "kind": "port",
+                               "cores": threads, "kind": "port",
                                "sample": "one DiT block at 1024^2 (4096 rows x 4224 keys) of the numpy oracle "
                                          "(restated inspect/ref_dit.py), %.2f s, scaled x%.1f block passes per picture"
                                          % (bs, LAYERS * (7 + (P + H * WW) / (H * WW)))}
@@ -371,10 +379,12 @@ def run_reference(args):
     if rank != 0:
         return None
     times = []
-    for i in range(args.warmup + args.steps):
-        bs = cpu_block_seconds()
-        if i >= args.warmup:
-            times.append(cpu_picture_seconds(bs))
+    with all_host_threads():
+        threads = cpu_threads()
+        for i in range(args.warmup + args.steps):
+            bs = cpu_block_seconds()
+            if i >= args.warmup:
+                times.append(cpu_picture_seconds(bs))
     sec = statistics.mean(times)
     v = 1.0 / sec
     return {
@@ -385,7 +395,7 @@ def run_reference(args):
         "config": {"workload": "BASELINE config 2: 1024^2 picture + 128 text rows, 8 Euler steps",
                    "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks", "global_batch": 1, "seq_len": P + H * WW,
                    "parallelism": "host CPU"},
-        "cpu_baseline": {"value": round(v, 6), "unit": "images/s", "cores": cpu_threads(), "kind": "port",
+        "cpu_baseline": {"value": round(v, 6), "unit": "images/s", "cores": threads, "kind": "port",
                          "sample": "each step one DiT block at 1024^2 (numpy oracle restating inspect/ref_dit.py; the "
                                    "reference's own ref_dit.py cannot travel to this box), scaled to a picture"},
         "e2e": {"value": round(v, 6), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

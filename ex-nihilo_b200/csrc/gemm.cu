@@ -17,6 +17,8 @@
 // :186-192, x_gelu_tanh :194-199) and the host Euler update
 // (src/generate.lisp:135) that followed illatio's GEMMs (src/cuda-dit.lisp
 // :115-130).
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "exn_device.cuh"
@@ -343,6 +345,178 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+
+// ----------------------------------------------------------------------------- CTA-pair kernel
+// A cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2
+// (M = 256): each CTA loads its own 128 rows of A and its half (128 rows) of
+// B per k-block, so per SM the tensor cores read 64 bytes of operands a clock
+// from shared memory and the TMA pulls half the B traffic of a 128 x 256 tile.
+// The leader (rank 0) issues the MMAs; each CTA's TMEM holds the fp32
+// accumulator of its 128 rows over all 256 columns and its own epilogue warps
+// drain it.  Barriers: full[] of the leader counts both CTAs' bytes; empty[]
+// and tfull[] are armed in both CTAs by multicast commits; tempty[] of the
+// leader counts the 8 epilogue warps of the pair.  No multicast loads.
+
+struct Gemm2Cfg {
+  static constexpr int BN = 256;
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
+  static constexpr int B_BYTES = 128 * BK * 2;   // this CTA's half of B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 512;           // two accumulators of 256 columns
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t IDESC = idesc_bf16(256, 256);
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+            int group_m, const GemmEpi ep, int* status) {
+  using C = Gemm2Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int num_m = (M + 255) / 256, num_n = N / C::BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = K / BK;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);     // the leader's producer, armed with both CTAs' bytes
+      mbar_init(&empty[s], 1);    // the leader's multicast commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);    // multicast commit
+      mbar_init(&tempty[a], 8);   // 4 epilogue warps x 2 CTAs (leader's instance used)
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, group_m, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lfull = mapa_shared(&full[stage], 0);
+          // the leader counts both CTAs' bytes; the peer's copies may land first (the phase
+          // cannot complete before the leader's arrival)
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * BK, mb * 256 + rank * 128);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * BK, nb * C::BN + rank * 128);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) __nanosleep(50000);  // copies already issued land before the CTA moves on
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer (leader only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, 1024);
+      const uint64_t b_desc0 = sdesc_sw128(smem_u32(sB), 16, 1024);
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = a_desc0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
+          const uint64_t bd = b_desc0 + static_cast<uint64_t>((stage * C::B_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) umma_pair(d_tmem, ad + 2 * k, bd + 2 * k, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit_pair(&tfull[acc], 0x3);
+      }
+      // every MMA issued has finished before either CTA releases its TMEM
+      umma_commit_pair(done, 0x3);
+      volatile int no_abort = 0;
+      mbar_wait(done, 0, &no_abort, nullptr, 0);
+    } else if (lane == 0 && rank == 1) {
+      volatile int no_abort = 0;  // the peer's copy of DONE is armed by the leader's commit
+      mbar_wait(done, 0, &no_abort, nullptr, 0);
+    }
+  } else {
+    // ---- epilogue warps 2..5 of each CTA: TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, group_m, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
+      tc_fence_after();
+      const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
+      epilogue<256, EPI>(taddr, row, row < M, nb * C::BN, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ----------------------------------------------------------------------------- host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -410,10 +584,60 @@ static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t
   return static_cast<int>(cudaGetLastError());
 }
 
+template <int EPI>
+static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
+  using C = Gemm2Cfg;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(k_gemm2<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  CUtensorMap ta, tb;
+  const uint64_t da[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(g.lda) * 2};
+  const uint32_t ba[2] = {BK, 128};
+  const uint64_t db[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(g.ldb) * 2};
+  const uint32_t bb[2] = {BK, 128};
+  if (make_tmap_bf16(&ta, g.a, 2, da, sa, ba) || make_tmap_bf16(&tb, g.b, 2, db, sb, bb)) return -4;
+  const int num_m = (g.M + 255) / 256;
+  const int tiles = num_m * (g.N / C::BN);
+  int clusters = num_sms / 2;
+  clusters = tiles < clusters ? tiles : clusters;
+  int group_m = static_cast<int>((48ll << 20) / (256ll * g.K * 2));
+  group_m = group_m < 4 ? 4 : group_m;
+  group_m = group_m > num_m ? num_m : group_m;
+  k_gemm2<EPI><<<clusters * 2, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, group_m, g.ep, d_status);
+  return static_cast<int>(cudaGetLastError());
+}
+
+static bool use_pairs() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("EXN_GEMM_PAIRS");
+    v = e ? atoi(e) : 1;
+  }
+  return v != 0;
+}
+
 int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK) return -1;
   if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b)) & 15) return -1;
   if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return -1;
+  if (use_pairs() && g.N % 256 == 0 && num_sms >= 2) {
+    switch (g.epi) {
+      case EPI_QKV:
+        if (g.ep.width % 256) return -1;
+        return launch_pair<EPI_QKV>(g, d_status, num_sms, st);
+      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU>(g, d_status, num_sms, st);
+      case EPI_GATE_RESID: return launch_pair<EPI_GATE_RESID>(g, d_status, num_sms, st);
+      case EPI_F32: return launch_pair<EPI_F32>(g, d_status, num_sms, st);
+      case EPI_BF16: return launch_pair<EPI_BF16>(g, d_status, num_sms, st);
+      case EPI_GELU_BF16: return launch_pair<EPI_GELU_BF16>(g, d_status, num_sms, st);
+      default: break;
+    }
+  }
   switch (g.epi) {
     case EPI_QKV:
       if (g.N % 256 || g.ep.width % 256) return -1;
