@@ -15,9 +15,11 @@
 //   warp 0      TMA: Q_a, Q_b once; K_j, V_j (128 keys x 128 dims, bf16)
 //   warp 1      tcgen05.mma: S_x = Q_x K_j^T into TMEM, O_x += P_x V_j
 //   warps 2..5  softmax of tile a, warps 6..9 of tile b: one query row per
-//               thread straight from TMEM (32x32b loads), P_x (bf16) into
-//               swizzled shared memory, O_x rescaled in TMEM only when the
-//               row maximum grows by more than 2^8
+//               thread straight from TMEM (32x32b loads); P_x (bf16, two per
+//               column) written back into TMEM over the first 64 columns of
+//               S_x and fed to the PV MMA from there (A operand in TMEM); O_x
+//               rescaled in TMEM only when the row maximum grows by more
+//               than 2^8
 // The MMA order PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) lets one tile's softmax
 // run while the tensor core serves the other.
 #include <stdlib.h>
@@ -36,12 +38,10 @@ constexpr int ATT_THREADS = 320;
 constexpr int TILE = 128;                 // queries per tile, keys per K/V tile
 constexpr int HALF = TILE * 128;          // bytes of one 64-column swizzled half of a 128 x 128 bf16 tile
 constexpr int TILE_BYTES = 2 * HALF;      // 32 KB
-// K_0 V_0 K_1 V_1 ... stream through a ring of 3 tile slots, so each load has
-// a slot free well before its MMA needs it (K_{j+1} reuses V_{j-1}'s slot,
-// V_{j+1} reuses K_j's).
-constexpr int SLOTS = 3;
-constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_SLOT = 2 * TILE_BYTES;
-constexpr int OFF_PA = (2 + SLOTS) * TILE_BYTES, OFF_PB = (3 + SLOTS) * TILE_BYTES, OFF_BAR = (4 + SLOTS) * TILE_BYTES;
+// K_0 V_0 K_1 V_1 ... stream through a ring of 4 tile slots, so each load has
+// a slot free well before its MMA needs it.
+constexpr int SLOTS = 4;
+constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_SLOT = 2 * TILE_BYTES, OFF_BAR = (2 + SLOTS) * TILE_BYTES;
 constexpr int ATT_SMEM = OFF_BAR + 256 + 1024;
 constexpr uint32_t IDESC_S = idesc_bf16(128, 128);
 constexpr uint32_t IDESC_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (dims contiguous)
@@ -155,8 +155,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const uint64_t dq_b = sdesc_sw128(smem_u32(smem + OFF_QB), 16, 1024);
       const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), 16, 1024);     // keys x dims, K-major
       const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), HALF, 1024);   // keys x dims read MN-major
-      const uint64_t dp_a = sdesc_sw128(smem_u32(smem + OFF_PA), 16, 1024);
-      const uint64_t dp_b = sdesc_sw128(smem_u32(smem + OFF_PB), 16, 1024);
       const uint32_t slot0 = smem_u32(smem + OFF_SLOT);
       auto issue_s = [&](uint64_t dq, uint32_t k_addr, uint32_t d) {
         const uint64_t dk = dk0 + static_cast<uint64_t>((k_addr - slot0) >> 4);
@@ -166,13 +164,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           umma_ss(d, dq + o, dk + o, IDESC_S, kk ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint64_t dp, uint32_t v_addr, uint32_t d, bool acc) {
+      // O_x += P_x V: P_x in TMEM at S_x's columns (8 columns = 16 keys per instruction)
+      auto issue_pv = [&](uint32_t p_tmem, uint32_t v_addr, uint32_t d, bool acc) {
         const uint64_t dv = dv0 + static_cast<uint64_t>((v_addr - slot0) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t o = static_cast<uint64_t>(((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
-          umma_ss(d, dp + o, dv + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV, (acc || kk) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(d, p_tmem + kk * 8, dv + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV, (acc || kk) ? 1u : 0u);
       };
       // wait for load T (K_{T/2} or V_{T/2}); its slot's address
       auto wait_load = [&](int t, uint32_t& addr) -> bool {
@@ -197,7 +194,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!(ok = wait_load(2 * j + 1, v_addr))) break;
         if (!(ok = mbar_wait(&bars->p_full[0], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(dp_a, v_addr, tmem + 256, j > 0);
+        issue_pv(tmem + 0, v_addr, tmem + 256, j > 0);
         if (!more) umma_commit(&bars->o_full[0]);
         if (more) {
           if (!(ok = wait_load(2 * j + 2, k_addr))) break;
@@ -207,7 +204,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         if (!(ok = mbar_wait(&bars->p_full[1], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
         tc_fence_after();
-        issue_pv(dp_b, v_addr, tmem + 384, j > 0);
+        issue_pv(tmem + 128, v_addr, tmem + 384, j > 0);
         umma_commit(&bars->slot_empty[(2 * j + 1) % SLOTS]);
         if (!more) umma_commit(&bars->o_full[1]);
         if (more) {
@@ -230,7 +227,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + x * 128;
     const uint32_t o_addr = tmem + lane_off + 256 + x * 128;
-    uint8_t* prow = smem + (x ? OFF_PB : OFF_PA) + r * 128;
     float m = -INFINITY, lsum = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -282,6 +278,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tmem_st_wait();
       }
       float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[64];  // P as bf16 pairs: key 2c and 2c+1 in column c
 #pragma unroll
       for (int c16 = 0; c16 < 16; ++c16) {
         float e[8];
@@ -291,13 +288,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           e[i] = i >= 8 - POLY ? exp2_fma(xv) : fast_exp2(xv);
           ps8[i] += e[i];
         }
-        const int half = c16 >> 3, cw = c16 & 7;
-        *reinterpret_cast<uint4*>(prow + half * HALF + ((cw ^ (r & 7)) << 4)) =
-            make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]), pack_bf16x2(e[4], e[5]),
-                       pack_bf16x2(e[6], e[7]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pk[c16 * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
       }
       lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-      fence_proxy_async_smem();
+      {
+        uint32_t half0[32], half1[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          half0[i] = pk[i];
+          half1[i] = pk[32 + i];
+        }
+        tmem_st32(s_addr, half0);
+        tmem_st32(s_addr + 32, half1);
+        tmem_st_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[x]);
