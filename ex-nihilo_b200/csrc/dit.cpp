@@ -16,6 +16,8 @@
 //     persist across steps without the reference's copies;
 //   * B independent pictures run as one batch of rows.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <chrono>
@@ -25,6 +27,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <thread>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -90,6 +94,72 @@ struct Profile {
   std::vector<std::pair<cudaEvent_t, int>> marks;  // event, category of the work after it
 };
 
+// NCCL, bound at run time to whichever libnccl.so.2 the process has (torch's,
+// or the system's); only its stable C API is used.
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) {
+      api.why = "libnccl.so.2 not found";
+      return;
+    }
+    bool ok = true;
+    auto sym = [&](const char* n) {
+      void* f = dlsym(lib, n);
+      if (!f) ok = false;
+      return f;
+    };
+    api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+    api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
+    api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+    api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
+    api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+    api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+    api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
+    api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
+    api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+    api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+    api.ok = ok;
+    if (!ok) api.why = "libnccl.so.2 lacks a symbol this library uses";
+  });
+  return api;
+}
+
+// buffers of a sequence-parallel (Ulysses) pass on one rank
+struct SpBufs {
+  void* mem = nullptr;
+  int cap_nloc = 0, cap_ntot = 0, cap_p = 0, cap_n = 0, cap_wg = 0;
+  float* xp = nullptr;       // every prefix row's x on step 1 [P][W]
+  bf16 *sq = nullptr, *sk = nullptr, *sv = nullptr;  // grouped send buffers [G][n_loc][Wg]
+  bf16* qf = nullptr;        // this rank's heads, every row of the pass [n_tot][Wg]
+  bf16* af = nullptr;        // attention out, same layout
+  bf16* ab = nullptr;        // attention out of this rank's rows, back by head group [G][n_loc][Wg]
+  float2* rope = nullptr;    // RoPE of this rank's rows [n_loc][64]
+  float* zslice = nullptr;   // [64][N/G]
+  float* zall = nullptr;     // [G][64][N/G]
+  bf16* kv = nullptr;        // [layer][K or V][L][Wg]: this rank's heads of the whole sequence
+  int kv_l = 0;
+};
+
 }  // namespace
 
 struct exn_handle {
@@ -137,6 +207,12 @@ struct exn_handle {
   Profile prof;
   double last_ms[3] = {0, 0, 0};
   long long launches = 0;  // kernels of this library queued by the step code since open
+
+  // sequence parallelism over `world` handles (one per GPU)
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  double comm_timeout_s = 60.0;
+  SpBufs sp;
 };
 
 namespace {
@@ -335,7 +411,7 @@ int check_tensor(exn_handle* h, const std::string& name, int type, const std::ve
 
 // ---------------------------------------------------------------------------- step buffers
 
-int ensure_buffers(exn_handle* h, int batch, int n, int l, int ptext, int nimg, int nref) {
+int ensure_buffers(exn_handle* h, int batch, int n, int l, int ptext, int nimg, int nref, bool with_kv = true) {
   const exn_config& c = h->cfg;
   const size_t W = c.width;
   // per-step activations
@@ -390,7 +466,7 @@ int ensure_buffers(exn_handle* h, int batch, int n, int l, int ptext, int nimg, 
     h->cap_nref = NR;
   }
   // K/V: [layers][2][batch][kv_l][W]; grown keeping the kept prompt rows
-  if (batch != h->kv_batch || l > h->kv_l) {
+  if (with_kv && (batch != h->kv_batch || l > h->kv_l)) {
     const int Lk = std::max(l, h->kv_l);
     const size_t bytes = static_cast<size_t>(c.layers) * 2 * batch * Lk * W * 2;
     bf16* nk = nullptr;
@@ -643,7 +719,312 @@ int run_step(exn_handle* h, const StepIn& in) {
   return EXN_OK;
 }
 
+
+// ---------------------------------------------------------------------------- sequence parallelism
+
+int nccl_fail(exn_handle* h, ncclResult_t r, const char* what) {
+  return fail(h, EXN_ECUDA, "%s: %s", what, nccl().GetErrorString ? nccl().GetErrorString(r) : "nccl error");
+}
+
+// a non-blocking communicator's queued work, or its init, settled (bounded by comm_timeout_s)
+int nccl_settle(exn_handle* h, ncclComm_t comm, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = nccl().CommGetAsyncError(comm, &st);
+    if (r != ncclSuccess) return nccl_fail(h, r, what);
+    if (st == ncclSuccess) return EXN_OK;
+    if (st != ncclInProgress) return nccl_fail(h, st, what);
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > h->comm_timeout_s) {
+      nccl().CommAbort(comm);
+      if (comm == h->comm) h->comm = nullptr;
+      return fail(h, EXN_ETIMEOUT, "%s: no progress in %.0f s, communicator aborted", what, h->comm_timeout_s);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
+  const exn_config& c = h->cfg;
+  const int G = h->world, W = c.width, Wg = W / G;
+  SpBufs& b = h->sp;
+  if (n_loc > b.cap_nloc || n_tot > b.cap_ntot || P > b.cap_p || N > b.cap_n || Wg != b.cap_wg) {
+    const int NL = std::max(n_loc, b.cap_nloc), NT = std::max(n_tot, b.cap_ntot), PP = std::max(P, b.cap_p),
+              NN = std::max(N, b.cap_n);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+      size_t o = off;
+      off += al(bytes);
+      return o;
+    };
+    const size_t oxp = take(size_t(std::max(PP, 1)) * W * 4), osq = take(size_t(NL) * W * 2),
+                 osk = take(size_t(NL) * W * 2), osv = take(size_t(NL) * W * 2), oqf = take(size_t(NT) * Wg * 2),
+                 oaf = take(size_t(NT) * Wg * 2), oab = take(size_t(NL) * W * 2), orp = take(size_t(NL) * 64 * 8),
+                 ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4);
+    if (b.mem) cudaFree(b.mem);
+    b.mem = nullptr;
+    CK(cudaMalloc(&b.mem, off));
+    char* m = static_cast<char*>(b.mem);
+    b.xp = reinterpret_cast<float*>(m + oxp);
+    b.sq = reinterpret_cast<bf16*>(m + osq);
+    b.sk = reinterpret_cast<bf16*>(m + osk);
+    b.sv = reinterpret_cast<bf16*>(m + osv);
+    b.qf = reinterpret_cast<bf16*>(m + oqf);
+    b.af = reinterpret_cast<bf16*>(m + oaf);
+    b.ab = reinterpret_cast<bf16*>(m + oab);
+    b.rope = reinterpret_cast<float2*>(m + orp);
+    b.zslice = reinterpret_cast<float*>(m + ozs);
+    b.zall = reinterpret_cast<float*>(m + oza);
+    b.cap_nloc = NL;
+    b.cap_ntot = NT;
+    b.cap_p = PP;
+    b.cap_n = NN;
+    b.cap_wg = Wg;
+  }
+  if (L > b.kv_l) {  // [layer][2][L][Wg], the kept prompt rows carried over
+    bf16* nk = nullptr;
+    CK(cudaMalloc(&nk, size_t(c.layers) * 2 * L * Wg * 2));
+    if (b.kv && h->prefix_valid && h->prefix_len > 0)
+      for (int i = 0; i < c.layers * 2; ++i)
+        CK(cudaMemcpyAsync(nk + size_t(i) * L * Wg, b.kv + size_t(i) * b.kv_l * Wg, size_t(h->prefix_len) * Wg * 2,
+                           cudaMemcpyDeviceToDevice, h->st));
+    else {
+      h->prefix_valid = false;
+      h->prefix_key = 0;
+    }
+    CK(cudaStreamSynchronize(h->st));
+    if (b.kv) cudaFree(b.kv);
+    b.kv = nk;
+    b.kv_l = L;
+  }
+  return EXN_OK;
+}
+
+void free_sp(exn_handle* h) {
+  if (h->sp.mem) cudaFree(h->sp.mem);
+  if (h->sp.kv) cudaFree(h->sp.kv);
+  h->sp = SpBufs();
+}
+
+// One DiT pass with this rank's share of the rows (Ulysses): every GEMM and
+// elementwise kernel on the rank's rows; before attention an all-to-all turns
+// [rows of this rank x all heads] into [all rows x this rank's heads]; after
+// it, back.  A rank holds prefix rows [r P/G, (r+1) P/G) (first pass only) and
+// image rows [r N/G, (r+1) N/G).  Its K/V cache holds its heads for every row,
+// so the prompt's K/V kept from the first pass stay sharded by head.
+int run_step_sp(exn_handle* h, const StepIn& in) {
+  const exn_config& c = h->cfg;
+  const int G = h->world, r = h->rank, W = c.width, Wg = W / G, heads = W / 128;
+  const int P = in.ptext + in.nref, N = in.hh * in.ww, L = P + N;
+  if (in.batch != 1) return fail(h, EXN_EINVAL, "sequence parallelism runs one picture at a time");
+  if (heads % G || Wg % 256 || P % G || N % G)
+    return fail(h, EXN_EINVAL,
+                "sequence parallelism over %d GPUs needs heads (%d), prefix rows (%d) and image rows (%d) divisible by "
+                "it and width / GPUs (%d) a multiple of 256",
+                G, heads, P, N, Wg);
+  const int pl = P / G, Nl = N / G;
+  const int pl_loc = in.cached ? 0 : pl;
+  const int n_loc = pl_loc + Nl, n_tot = in.cached ? N : L, q0 = in.cached ? P : 0;
+  const int img0 = in.cached ? 0 : P;  // first image row in qf / af
+  int rc;
+  if ((rc = ensure_buffers(h, 1, std::max(n_loc, 1), L, std::max(in.ptext, 1), N, in.nref, false))) return rc;
+  if ((rc = ensure_sp(h, n_loc, n_tot, P, N, L))) return rc;
+  SpBufs& b = h->sp;
+  const size_t kv_layer = size_t(2) * b.kv_l * Wg;
+  h->launches += 5 + 3 + 8LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
+
+  // timestep
+  temb_launch(h->emb, in.sigma, c.freq, h->st);
+  gemv_launch(h->lin1.kind, h->lin1.w, h->lin1.d, h->emb, h->e1, 2, c.freq, W, 1, 0, h->st);
+  gemv_launch(h->lin2.kind, h->lin2.w, h->lin2.d, h->e1, h->e2, 2, W, W, 1, 0, h->st);
+  gemv_launch(h->mod.kind, h->mod.w, h->mod.d, h->e2, h->modv, 2, W, 4 * W, 2, W, h->st);
+  gemv_launch(h->nout.kind, h->nout.w, h->nout.d, h->e2, h->sc, 1, W, W, 0, 0, h->st);
+  // first pass: every prefix row through txt_in (and an edit's picture through img_in), this rank's slice kept
+  if (!in.cached) {
+    if (in.ptext > 0) {
+      rms_launch(in.ctx, h->txt_norm, h->ctxn, in.ptext, c.context, h->st);
+      GemmEpi e1;
+      e1.out = h->tin;
+      e1.ld_out = W;
+      if ((rc = gemm(h, h->ctxn, c.context, h->w_txt_in, c.context, in.ptext, W, c.context, EPI_GELU_BF16, e1)))
+        return rc;
+      GemmEpi e2;
+      e2.out = b.xp;
+      e2.ld_out = W;
+      e2.split_at = in.nref ? in.a : (1 << 30);
+      e2.split_gap = in.nref;
+      if ((rc = gemm(h, h->tin, W, h->w_txt_out, W, in.ptext, W, W, EPI_F32, e2))) return rc;
+    }
+    if (in.nref) {
+      latent_rows_launch(in.ref, h->ref_rows, 1, c.latent, in.nref, h->st);
+      GemmEpi er;
+      er.out = b.xp;
+      er.ld_out = W;
+      er.off = in.a;
+      if ((rc = gemm(h, h->ref_rows, c.latent, h->w_img_in, c.latent, in.nref, W, c.latent, EPI_F32, er))) return rc;
+    }
+    CK(cudaMemcpyAsync(h->x, b.xp + size_t(r) * pl * W, size_t(pl) * W * 4, cudaMemcpyDeviceToDevice, h->st));
+  }
+  // this rank's image rows: latent columns [r N/G, (r+1) N/G)
+  latent_rows_launch(in.lat, h->lat_rows, 1, c.latent, Nl, h->st, N, r * Nl);
+  {
+    GemmEpi ei;
+    ei.out = h->x;
+    ei.ld_out = W;
+    ei.off = pl_loc;
+    if ((rc = gemm(h, h->lat_rows, c.latent, h->w_img_in, c.latent, Nl, W, c.latent, EPI_F32, ei))) return rc;
+  }
+  if (pl_loc > 0)
+    rope_table_launch(b.rope, r * pl, n_loc, P, in.hh, in.ww, in.nref ? in.a : 0, in.nref ? in.rh : 0,
+                      in.nref ? in.rw : 0, h->st, pl_loc, P + r * Nl);
+  else
+    rope_table_launch(b.rope, P + r * Nl, n_loc, P, in.hh, in.ww, in.nref ? in.a : 0, in.nref ? in.rh : 0,
+                      in.nref ? in.rw : 0, h->st);
+
+  NcclApi& nc = nccl();
+  const size_t chunk = size_t(n_loc) * Wg;  // elements of one rank-to-rank piece of a grouped buffer
+  auto bytes = [](size_t elems) { return elems * 2; };
+  for (int il = 0; il < c.layers; ++il) {
+    bf16* kl = b.kv + il * kv_layer;
+    bf16* vl = kl + size_t(b.kv_l) * Wg;
+    ln_mod_launch(h->x, h->y, h->modv + 0 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
+    GemmEpi eq;
+    eq.seg_in = n_loc;
+    eq.width = W;
+    eq.norm_q = h->norm_q + il * c.head_dim;
+    eq.norm_k = h->norm_k + il * c.head_dim;
+    eq.rope = b.rope;
+    eq.q = b.sq;
+    eq.k = b.sk;
+    eq.v = b.sv;
+    eq.group_w = Wg;
+    if ((rc = gemm(h, h->y, W, h->w_qkv + static_cast<size_t>(il) * 3 * W * W, W, n_loc, 3 * W, W, EPI_QKV, eq)))
+      return rc;
+    // all-to-all: my rows' head group s to rank s; rank s's rows of my head group into every row's place
+    nc.GroupStart();
+    for (int sr = 0; sr < G; ++sr) {
+      const bf16* src[3] = {b.sq + sr * chunk, b.sk + sr * chunk, b.sv + sr * chunk};
+      bf16* dst_pre[3] = {b.qf + size_t(sr) * pl * Wg, kl + size_t(sr) * pl * Wg, vl + size_t(sr) * pl * Wg};
+      bf16* dst_img[3] = {b.qf + size_t(img0 + sr * Nl) * Wg, kl + size_t(P + sr * Nl) * Wg, vl + size_t(P + sr * Nl) * Wg};
+      for (int t = 0; t < 3; ++t) {
+        if (pl_loc) {
+          nc.Send(src[t], bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
+          nc.Recv(dst_pre[t], bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
+        }
+        nc.Send(src[t] + size_t(pl_loc) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
+        nc.Recv(dst_img[t], bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
+      }
+    }
+    nc.GroupEnd();
+    if ((rc = nccl_settle(h, h->comm, "all-to-all before attention"))) return rc;
+    AttnArgs aa;
+    aa.q = b.qf;
+    aa.k = kl;
+    aa.v = vl;
+    aa.out = b.af;
+    aa.nq = n_tot;
+    aa.q0 = q0;
+    aa.p = P;
+    aa.l = L;
+    aa.b0 = in.nref ? in.a : 0;
+    aa.b1 = in.nref ? in.a + in.nref : 0;
+    aa.heads = heads / G;
+    aa.width = Wg;
+    aa.kv_rows = b.kv_l;
+    aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
+    // all-to-all back: rank s's rows of my heads to s; my rows of rank s's heads into group s
+    nc.GroupStart();
+    for (int sr = 0; sr < G; ++sr) {
+      bf16* back = b.ab + sr * chunk;
+      if (pl_loc) {
+        nc.Send(b.af + size_t(sr) * pl * Wg, bytes(size_t(pl) * Wg), ncclUint8, sr, h->comm, h->st);
+        nc.Recv(back, bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
+      }
+      nc.Send(b.af + size_t(img0 + sr * Nl) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
+      nc.Recv(back + size_t(pl_loc) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
+    }
+    nc.GroupEnd();
+    if ((rc = nccl_settle(h, h->comm, "all-to-all after attention"))) return rc;
+    group_gather_launch(b.ab, h->att, G, n_loc, Wg, h->st);
+    GemmEpi eo;
+    eo.out = h->x;
+    eo.ld_out = W;
+    eo.seg_in = n_loc;
+    eo.mod = h->modv + 1 * W;
+    eo.mod_stride = 4 * W;
+    eo.n0 = 0;
+    eo.p = pl_loc;
+    if ((rc = gemm(h, h->att, W, h->w_out + static_cast<size_t>(il) * W * W, W, n_loc, W, W, EPI_GATE_RESID, eo)))
+      return rc;
+    ln_mod_launch(h->x, h->y, h->modv + 2 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
+    GemmEpi eg;
+    eg.out = h->ff;
+    eg.ld_out = c.ffn;
+    if ((rc = gemm(h, h->y, W, h->w_gu + static_cast<size_t>(il) * 2 * c.ffn * W, W, n_loc, 2 * c.ffn, W, EPI_SWIGLU,
+                   eg)))
+      return rc;
+    GemmEpi ed = eo;
+    ed.mod = h->modv + 3 * W;
+    if ((rc = gemm(h, h->ff, c.ffn, h->w_down + static_cast<size_t>(il) * W * c.ffn, c.ffn, n_loc, W, c.ffn,
+                   EPI_GATE_RESID, ed)))
+      return rc;
+  }
+  // this rank's image rows: LayerNorm * (1 + sc), proj_out into its latent columns
+  ln_mod_launch(h->x, h->y, h->sc, 0, Nl, W, Nl, n_loc, pl_loc, 0, 0, 1, h->st);
+  GemmEpi ep;
+  ep.z = in.z ? in.z + size_t(r) * Nl : nullptr;
+  ep.vout = in.v ? in.v + size_t(r) * Nl : nullptr;
+  ep.dsigma = in.dsigma;
+  ep.nimg = Nl;
+  ep.zstride = N;
+  if ((rc = gemm(h, h->y, W, h->w_proj, W, Nl, c.latent, W, EPI_PROJ, ep))) return rc;
+  CK(cudaGetLastError());
+  return EXN_OK;
+}
+
+// every rank's latent columns [s N/G, (s+1) N/G) of Z (64 x N) gathered into every rank's Z
+int sp_gather_columns(exn_handle* h, float* z, int N) {
+  const int G = h->world, r = h->rank, Nl = N / G;
+  SpBufs& b = h->sp;
+  CK(cudaMemcpy2DAsync(b.zslice, size_t(Nl) * 4, z + size_t(r) * Nl, size_t(N) * 4, size_t(Nl) * 4, 64,
+                       cudaMemcpyDeviceToDevice, h->st));
+  ncclResult_t nr = nccl().AllGather(b.zslice, b.zall, size_t(64) * Nl, ncclFloat32, h->comm, h->st);
+  if (nr != ncclSuccess && nr != ncclInProgress) return nccl_fail(h, nr, "all-gather of the latent");
+  int rc;
+  if ((rc = nccl_settle(h, h->comm, "all-gather of the latent"))) return rc;
+  for (int s = 0; s < G; ++s)
+    CK(cudaMemcpy2DAsync(z + size_t(s) * Nl, size_t(N) * 4, b.zall + size_t(s) * 64 * Nl, size_t(Nl) * 4,
+                         size_t(Nl) * 4, 64, cudaMemcpyDeviceToDevice, h->st));
+  return EXN_OK;
+}
+
+int run_pass(exn_handle* h, const StepIn& in) {
+  return (h->comm && h->world > 1) ? run_step_sp(h, in) : run_step(h, in);
+}
+
 int check_status(exn_handle* h) {
+  if (h->comm) {  // a peer that stopped answering must not hang this rank: poll with a deadline
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+      const cudaError_t q = cudaStreamQuery(h->st);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) CK(q);
+      ncclResult_t st = ncclSuccess;
+      nccl().CommGetAsyncError(h->comm, &st);
+      if (st != ncclSuccess && st != ncclInProgress) {
+        nccl().CommAbort(h->comm);
+        h->comm = nullptr;
+        return nccl_fail(h, st, "communicator failed");
+      }
+      if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > h->comm_timeout_s) {
+        nccl().CommAbort(h->comm);
+        h->comm = nullptr;
+        return fail(h, EXN_ETIMEOUT, "no progress in %.0f s; communicator aborted", h->comm_timeout_s);
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+  }
   CK(cudaStreamSynchronize(h->st));
   int s = 0;
   CK(cudaMemcpy(&s, h->d_status, sizeof s, cudaMemcpyDeviceToHost));
@@ -672,7 +1053,7 @@ int upload_inputs(exn_handle* h, const float* context, int p, const float* laten
   const exn_config& c = h->cfg;
   const int nimg = hh * ww, nref = ref ? ref->rh * ref->rw : 0;
   int rc;
-  if ((rc = ensure_buffers(h, 1, (p + nref + nimg), p + nref + nimg, p, nimg, nref))) return rc;
+  if ((rc = ensure_buffers(h, 1, (p + nref + nimg), p + nref + nimg, p, nimg, nref, h->comm == nullptr))) return rc;
   if (need_ctx && p) CK(cudaMemcpyAsync(h->ctx_dev, context, size_t(p) * c.context * 4, cudaMemcpyHostToDevice, h->st));
   if (need_ctx && nref)
     CK(cudaMemcpyAsync(h->ref_dev, ref->latent, size_t(nref) * c.latent * 4, cudaMemcpyHostToDevice, h->st));
@@ -749,6 +1130,8 @@ void exn_close(exn_handle* h) {
   cudaSetDevice(h->cfg.device);
   if (h->st) cudaStreamSynchronize(h->st);
   free_buffers(h);
+  free_sp(h);
+  if (h->comm) nccl().CommDestroy(h->comm);
   for (void* p : h->extra_allocs) cudaFree(p);
   if (h->slab) cudaFree(h->slab);
   if (h->d_status) cudaFree(h->d_status);
@@ -959,7 +1342,7 @@ int exn_velocity(exn_handle* h, const float* context, int p, const float* latent
   if ((rc = use_device(h)) || (rc = check_step_args(h, 1, p, hh, ww, ref))) return rc;
   const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
   const bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len &&
-                      h->kv_batch == 1;
+                      (h->comm ? true : h->kv_batch == 1);
   if ((rc = upload_inputs(h, context, p, latent, hh, ww, ref, !cached))) return rc;
   if (!cached) {
     h->prefix_valid = false;
@@ -979,7 +1362,8 @@ int exn_velocity(exn_handle* h, const float* context, int p, const float* latent
   in.ref = h->ref_dev;
   in.lat = h->lat_dev;
   in.v = h->vout;
-  if ((rc = run_step(h, in))) return rc;
+  if ((rc = run_pass(h, in))) return rc;
+  if (h->comm && h->world > 1 && (rc = sp_gather_columns(h, h->vout, hh * ww))) return rc;
   CK(cudaMemcpyAsync(v_out, h->vout, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
   if ((rc = check_status(h))) return rc;
   if (prefix_key && !cached) {
@@ -997,7 +1381,8 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
   int rc;
   if ((rc = use_device(h)) || (rc = check_step_args(h, 1, p, hh, ww, ref))) return rc;
   const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
-  bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len && h->kv_batch == 1;
+  bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len &&
+                (h->comm ? true : h->kv_batch == 1);
   if ((rc = upload_inputs(h, context, p, z, hh, ww, ref, true))) return rc;
   for (int s = 0; s + 1 < nsig; ++s) {
     if (!cached) {
@@ -1019,7 +1404,7 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
     in.lat = h->lat_dev;
     in.z = h->lat_dev;
     in.dsigma = static_cast<float>(sigmas[s + 1] - sigmas[s]);
-    if ((rc = run_step(h, in))) return rc;
+    if ((rc = run_pass(h, in))) return rc;
     if (!cached && prefix_key) {
       h->prefix_key = prefix_key;
       h->prefix_len = pfx;
@@ -1027,6 +1412,7 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
       cached = true;
     }
   }
+  if (h->comm && h->world > 1 && (rc = sp_gather_columns(h, h->lat_dev, hh * ww))) return rc;
   CK(cudaMemcpyAsync(z, h->lat_dev, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
   if ((rc = check_status(h))) {
     h->prefix_valid = false;
@@ -1039,6 +1425,8 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
 static int generate_dev(exn_handle* h, int batch, const float* d_ctx, int p, float* d_z, int hh, int ww,
                         const double* sigmas, int nsig) {
   int rc;
+  if (h->comm) return fail(h, EXN_EINVAL, "batched pictures run one per handle; this handle shares its rows over %d GPUs",
+                           h->world);
   h->prefix_valid = false;
   h->prefix_key = 0;
   for (int s = 0; s + 1 < nsig; ++s) {
@@ -1110,6 +1498,57 @@ int exn_release(exn_handle* h) {
   if ((rc = use_device(h))) return rc;
   CK(cudaStreamSynchronize(h->st));
   free_buffers(h);
+  free_sp(h);
+  return EXN_OK;
+}
+
+int exn_comm_unique_id(void* id) {
+  if (!id) return fail(nullptr, EXN_EINVAL, "exn_comm_unique_id: null buffer");
+  NcclApi& nc = nccl();
+  if (!nc.ok) return fail(nullptr, EXN_EUNSUPPORTED, "NCCL: %s", nc.why.c_str());
+  ncclUniqueId u;
+  const ncclResult_t r = nc.GetUniqueId(&u);
+  if (r != ncclSuccess) return fail(nullptr, EXN_ECUDA, "ncclGetUniqueId: %s", nc.GetErrorString(r));
+  std::memcpy(id, &u, sizeof u);
+  return EXN_OK;
+}
+
+int exn_comm_init(exn_handle* h, const void* id, int rank, int world) {
+  if (!h || !id || world < 1 || rank < 0 || rank >= world) return fail(h, EXN_EINVAL, "exn_comm_init: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  NcclApi& nc = nccl();
+  if (!nc.ok) return fail(h, EXN_EUNSUPPORTED, "NCCL: %s", nc.why.c_str());
+  if (h->comm) return fail(h, EXN_EINVAL, "exn_comm_init: the handle already has a communicator");
+  if (const char* t = std::getenv("EXN_COMM_TIMEOUT_S")) h->comm_timeout_s = std::max(1.0, std::atof(t));
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof u);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;  // every wait on it is bounded (nccl_settle, check_status)
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = nc.CommInitRankConfig(&comm, world, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) return fail(h, EXN_ECUDA, "ncclCommInitRankConfig: %s", nc.GetErrorString(r));
+  if ((rc = nccl_settle(h, comm, "communicator init"))) return rc;
+  h->comm = comm;
+  h->rank = rank;
+  h->world = world;
+  h->prefix_valid = false;  // the kept prompt K/V now live per head shard
+  h->prefix_key = 0;
+  return EXN_OK;
+}
+
+int exn_comm_destroy(exn_handle* h) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_comm_destroy: null handle");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  CK(cudaStreamSynchronize(h->st));
+  if (h->comm) nccl().CommDestroy(h->comm);
+  h->comm = nullptr;
+  h->rank = 0;
+  h->world = 1;
+  free_sp(h);
+  h->prefix_valid = false;
+  h->prefix_key = 0;
   return EXN_OK;
 }
 

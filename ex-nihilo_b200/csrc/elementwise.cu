@@ -110,14 +110,15 @@ __global__ void __launch_bounds__(LN_THREADS) k_rms(const float* __restrict__ x,
   }
 }
 
-// lat [B][C][n] -> rows [B*n][C], 32 x 32 tiles through shared memory
-__global__ void k_latent_rows(const float* __restrict__ lat, bf16* __restrict__ rows, int channels, int n) {
+// lat [B][C][ld], columns col0.. -> rows [B*n][C], 32 x 32 tiles through shared memory
+__global__ void k_latent_rows(const float* __restrict__ lat, bf16* __restrict__ rows, int channels, int n, int ld,
+                              int col0) {
   __shared__ float tile[32][33];
   const int b = blockIdx.z, i0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  const float* src = lat + static_cast<long long>(b) * channels * n;
+  const float* src = lat + static_cast<long long>(b) * channels * ld + col0;
   for (int k = threadIdx.y; k < 32; k += 8) {
     const int c = c0 + k, i = i0 + threadIdx.x;
-    tile[k][threadIdx.x] = (c < channels && i < n) ? src[static_cast<long long>(c) * n + i] : 0.f;
+    tile[k][threadIdx.x] = (c < channels && i < n) ? src[static_cast<long long>(c) * ld + i] : 0.f;
   }
   __syncthreads();
   bf16* dst = rows + static_cast<long long>(b) * n * channels;
@@ -131,11 +132,11 @@ __global__ void k_latent_rows(const float* __restrict__ lat, bf16* __restrict__ 
 // one thread per (row, pair); pairs 0..7 axis 0 (16 dims), 8..35 axis 1,
 // 36..63 axis 2 (56 each); theta 10000, angles in double.
 __global__ void k_rope_table(float2* __restrict__ table, int r0, int count, int p, int h, int w, int ra, int rh,
-                             int rw) {
+                             int rw, int split, int r1) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= count * 64) return;
   const int i = idx >> 6, j = idx & 63;
-  const int g = r0 + i;
+  const int g = split > 0 ? (i < split ? r0 + i : r1 + (i - split)) : r0 + i;
   int pos[3];
   auto image = [&](int frame, int k, int hh, int ww) {
     const int rr = k / ww, cc = k - (k / ww) * ww;
@@ -410,16 +411,35 @@ void rms_launch(const float* x, const float* w, bf16* y, int rows, int width, cu
   k_rms<<<rows, LN_THREADS, 0, st>>>(x, w, y, rows, width);
 }
 
-void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, int n, cudaStream_t st) {
+void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, int n, cudaStream_t st, int ld,
+                        int i0) {
   dim3 grid((n + 31) / 32, (channels + 31) / 32, batch);
-  k_latent_rows<<<grid, dim3(32, 8), 0, st>>>(lat, rows, channels, n);
+  k_latent_rows<<<grid, dim3(32, 8), 0, st>>>(lat, rows, channels, n, ld > 0 ? ld : n, i0);
 }
 
 void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, int ref_a, int ref_h, int ref_w,
-                       cudaStream_t st) {
+                       cudaStream_t st, int split, int r1) {
   if (count <= 0) return;
   k_rope_table<<<blocks_for(static_cast<long long>(count) * 64, 256), 256, 0, st>>>(table, r0, count, p, h, w, ref_a,
-                                                                                    ref_h, ref_w);
+                                                                                    ref_h, ref_w, split, r1);
+}
+
+// in [G][n][gw] -> out [n][G*gw], 16 bytes a thread
+__global__ void k_group_gather(const uint4* __restrict__ in, uint4* __restrict__ out, int groups, int n, int gw8) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(groups) * n * gw8;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % gw8);
+  const long long rest = idx / gw8;
+  const int t = static_cast<int>(rest % n), g = static_cast<int>(rest / n);
+  out[(static_cast<long long>(t) * groups + g) * gw8 + c] = in[idx];
+}
+
+void group_gather_launch(const bf16* in, bf16* out, int groups, int n, int gw, cudaStream_t st) {
+  const long long total = static_cast<long long>(groups) * n * (gw / 8);
+  if (total <= 0) return;
+  k_group_gather<<<blocks_for(total, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out),
+                                                         groups, n, gw / 8);
 }
 
 void temb_launch(float* emb, double sigma, int freq, cudaStream_t st) {

@@ -42,11 +42,15 @@ struct GemmEpi {
   bf16* k = nullptr;
   bf16* v = nullptr;
   long long kv_sample_stride = 0;  // elements from one sample's K (V) rows to the next
+  // EPI_QKV, sequence-parallel: when group_w > 0, q, k and v are all written head-group-major,
+  // [world][seg_in rows][group_w], the layout an all-to-all sends whole (group g to rank g)
+  int group_w = 0;
   // EPI_PROJ
   float* z = nullptr;
   float* vout = nullptr;
   float dsigma = 0.f;
-  int nimg = 0;
+  int nimg = 0;        // image rows of a sample in this GEMM
+  int zstride = 0;     // floats between channels of v / z (0: nimg)
 };
 
 struct GemmArgs {
@@ -81,11 +85,16 @@ void ln_mod_launch(const float* x, bf16* y, const float* scale, int mod_stride, 
                    int seg_out, int off, int n0, int p, int single, cudaStream_t st);
 // y = RMSNorm(x) * w (w already 1 + text_norm), bf16 out
 void rms_launch(const float* x, const float* w, bf16* y, int rows, int width, cudaStream_t st);
-// latent [B][C][n] f32 channel-major -> rows [B*n][C] bf16
-void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, int n, cudaStream_t st);
-// RoPE (cos, sin) of rows r0 .. r0+count of the sequence (host.lisp's positions), [count][64]
+// latent [B][C][ld] f32 channel-major, columns i0 .. i0+n -> rows [B*n][C] bf16
+void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, int n, cudaStream_t st, int ld = 0,
+                        int i0 = 0);
+// RoPE (cos, sin) of rows r0 .. r0+count of the sequence (host.lisp's positions), [count][64].
+// With split > 0 the table's rows are a rank's shard instead: local row t < split is sequence row
+// r0 + t (prefix), t >= split is sequence row r1 + (t - split) (image).
 void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, int ref_a, int ref_h, int ref_w,
-                       cudaStream_t st);
+                       cudaStream_t st, int split = 0, int r1 = 0);
+// in [G][n][gw] -> out [n][G*gw] (head groups back into columns), bf16
+void group_gather_launch(const bf16* in, bf16* out, int groups, int n, int gw, cudaStream_t st);
 // emb[2][freq]: timestep embedding of 1000*sigma and of 0
 void temb_launch(float* emb, double sigma, int freq, cudaStream_t st);
 // Weight kinds for the small GEMVs

@@ -142,7 +142,10 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
     const int hc0 = col0 - sec * e.width;      // first column within q / k / v
     const int t = row % e.seg_in, b = row / e.seg_in;
     bf16* dst;
-    if (sec == 0)
+    if (e.group_w > 0)
+      dst = (sec == 0 ? e.q : sec == 1 ? e.k : e.v) +
+            (static_cast<long long>(hc0 / e.group_w) * e.seg_in + row) * e.group_w + hc0 % e.group_w;
+    else if (sec == 0)
       dst = e.q + static_cast<long long>(row) * e.width + hc0;
     else
       dst = (sec == 1 ? e.k : e.v) + b * e.kv_sample_stride + static_cast<long long>(e.n0 + t) * e.width + hc0;
@@ -179,7 +182,8 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
   } else if constexpr (EPI == EPI_PROJ) {
     static_assert(BN == 64, "proj_out has the latent's 64 channels");
     const int b = row / e.nimg, i = row - (row / e.nimg) * e.nimg;
-    const long long base = static_cast<long long>(b) * 64 * e.nimg + i;
+    const int zs = e.zstride > 0 ? e.zstride : e.nimg;
+    const long long base = static_cast<long long>(b) * 64 * zs + i;
 #pragma unroll 1
     for (int c = 0; c < 64; c += 32) {
       uint32_t r[32];
@@ -187,7 +191,7 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
       if (!valid) continue;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const long long idx = base + static_cast<long long>(c + j) * e.nimg;
+        const long long idx = base + static_cast<long long>(c + j) * zs;
         const float val = __uint_as_float(r[j]);
         if (e.vout) e.vout[idx] = val;
         if (e.z) e.z[idx] += e.dsigma * val;

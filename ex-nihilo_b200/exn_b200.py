@@ -90,6 +90,9 @@ def lib():
                                                ctypes.POINTER(ctypes.c_double), ctypes.c_int, vp]),
         "exn_sync": (ctypes.c_int, [H]),
         "exn_release": (ctypes.c_int, [H]),
+        "exn_comm_unique_id": (ctypes.c_int, [vp]),
+        "exn_comm_init": (ctypes.c_int, [H, vp, ctypes.c_int, ctypes.c_int]),
+        "exn_comm_destroy": (ctypes.c_int, [H]),
         # testing entry points (include/exn_b200_testing.h)
         "exn_test_gemm": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
@@ -131,6 +134,15 @@ def prefix_key_of(key) -> int:
         return key
     h = int.from_bytes(hashlib.blake2b(repr(key).encode(), digest_size=8).digest(), "little")
     return h or 1
+
+
+def comm_unique_id() -> bytes:
+    """An NCCL unique id (128 bytes) for exn_comm_init: made once, passed to every rank."""
+    buf = ctypes.create_string_buffer(128)
+    rc = lib().exn_comm_unique_id(buf)
+    if rc != EXN_OK:
+        raise ExnError(rc, lib().exn_last_error(None).decode(errors="replace"))
+    return buf.raw
 
 
 def default_config(**kw) -> Config:
@@ -247,6 +259,14 @@ class Dit:
 
     def release(self):
         self._ck(lib().exn_release(self.h))
+
+    def comm_init(self, uid: bytes, rank: int, world: int):
+        """Share this picture's rows with WORLD ranks (sequence parallelism, NCCL all-to-all)."""
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        self._ck(lib().exn_comm_init(self.h, buf, rank, world))
+
+    def comm_destroy(self):
+        self._ck(lib().exn_comm_destroy(self.h))
 
     def profile(self, on=True):
         self._ck(lib().exn_test_profile(self.h, 1 if on else 0))

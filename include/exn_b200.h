@@ -137,6 +137,22 @@ int exn_sync(exn_handle* h);
 /* dit-release: free the step buffers and the kept prompt keys and values. */
 int exn_release(exn_handle* h);
 
+/* Sequence parallelism over GPUs for one long picture (an edit, a large
+ * canvas): WORLD handles, one per GPU and process, join one NCCL
+ * communicator; afterwards exn_velocity and exn_generate, called with the
+ * same arguments on every rank, split the rows of the pass across the ranks
+ * (prefix and image rows in equal shares), exchange Q/K/V and the attention
+ * output by all-to-all (Ulysses: attention on heads/WORLD heads per rank),
+ * keep the prompt's K/V per head shard, and return the full result on every
+ * rank.  Needs heads, prefix rows and image rows divisible by WORLD and
+ * width/WORLD a multiple of 256.  No counterpart in the reference (one GPU;
+ * src/server.lisp:24-28).  Every wait on the communicator is bounded by
+ * EXN_COMM_TIMEOUT_S (default 60 s), after which it is aborted and the call
+ * returns EXN_ETIMEOUT. */
+int exn_comm_unique_id(void* id128);  /* 128 bytes: rank 0 makes it, every rank passes the same */
+int exn_comm_init(exn_handle* h, const void* id128, int rank, int world);
+int exn_comm_destroy(exn_handle* h);
+
 #ifdef __cplusplus
 }
 #endif
