@@ -68,6 +68,24 @@ def picture_flops(batch=1, layers=LAYERS):
     return batch * g, batch * a
 
 
+def edit_flops(layers=LAYERS, p_text=512, a=8, rh=64, rw=64, h=H, w=WW):
+    """Algorithmic FLOPs of one 8-step edit picture: the prefix is the text's
+    p_text rows with the reference picture's rh*rw rows after its first A (src/host.lisp:37-50),
+    masked as src/cuda/dit.cu:60-66 (xa_lim)."""
+    nref, n = rh * rw, h * w
+    p = p_text + nref
+    l = p + n
+    g = np.arange(p)
+    lim = np.where((g >= a) & (g < a + nref), a + nref - 1, g)
+    prefix_pairs = float((lim + 1).sum())
+    per_row = 2.0 * (3 * W * W + W * W + 2 * FFN * W + FFN * W) * layers
+    gemm1 = per_row * l + 2.0 * n * LAT * W * 2 + 2.0 * p_text * (CTX * W + W * W) + 2.0 * nref * LAT * W
+    gemm2 = per_row * n + 2.0 * n * LAT * W * 2
+    attn1 = 4.0 * 128 * HEADS * (prefix_pairs + n * l) * layers
+    attn2 = 4.0 * 128 * HEADS * (n * l) * layers
+    return gemm1 + 7 * gemm2, attn1 + 7 * attn2
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -374,6 +392,62 @@ def run_exn(args):
     return out
 
 
+def run_edit(args):
+    """one edit picture (4096 target rows, a 4096-row reference picture and 512 text
+    rows: 8704 rows) through all N GPUs at once (Ulysses sequence parallelism), 8 Euler steps; a new
+    edit (a new prompt key) each step.  Timed through exn_generate (host buffers: 10 MB in, 1 MB out)."""
+    import torch
+    import exn_b200 as E
+    from oracle import dit_oracle as O
+    rank, world, local, dist = init_dist(args.gpus)
+    torch.cuda.set_device(local)
+    d = E.Dit(device=local, layers=args.layers)
+    d.load_synthetic(1)
+    if world > 1:
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        d.comm_init(obj[0], rank, world)
+    p_text, a = 512, 8
+    ctx, lat = O.synth_inputs(O.Shape(), p_text, H, WW, seed=7)
+    _, ref = O.synth_inputs(O.Shape(), 1, H, WW, seed=8)
+    refarg = (a, ref[0], H, WW)
+    for i in range(args.warmup):
+        d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("warm", i), ref=refarg)
+    barrier(dist)
+    with Clocks(gpu_index(local)) as clk:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            z = d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("edit", i), ref=refarg)
+        dt = (time.perf_counter() - t0) / args.steps
+    ms = max_over_ranks(dist, dt * 1e3)
+    launches = d.launch_count()
+    if world > 1:
+        d.comm_destroy()
+    d.close()
+    barrier(dist)
+    if rank != 0:
+        return None
+    bt_burst, bt, hbm, src = peaks()
+    gf, af = edit_flops(args.layers)
+    value = 1e3 / ms
+    return {
+        "metric": METRIC, "value": round(value, 4), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init Q8_0 weights (seed 1, bf16 in HBM); text, reference and noise ~N(0,1)",
+        "config": {"workload": "BASELINE config 4: edit, 4096 target + 4096 reference + 512 text rows (8704), A=8, "
+                               "8 Euler steps, one picture over all GPUs (Ulysses, NCCL all-to-all)",
+                   "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks, FFN 12288", "global_batch": 1, "seq_len": 8704,
+                   "parallelism": "sp%d (Ulysses)" % world, "timing": "wall clock around exn_generate (host buffers)",
+                   "algorithmic_tflop_per_picture": round((gf + af) / 1e12, 1)},
+        "tc_peak_frac": round((gf + af) / (ms * 1e-3) / world / 1e12 / bt, 4),
+        "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": (p_text * CTX + 2 * LAT * H * WW) * 4,
+                "d2h_bytes_per_step": LAT * H * WW * 4},
+        "clocks": clk.summary(),
+        "gpu_launches": launches,
+    }
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
@@ -413,15 +487,27 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class event timing")
     ap.add_argument("--layers", type=int, default=LAYERS, help="blocks (profiling cases only; the bench is 32)")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg5"],
-                    help="cfg2: one picture per GPU per step (default); cfg5: 64 pictures split over the GPUs")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4", "cfg5"],
+                    help="cfg2: one picture per GPU per step (default); cfg4: one 8704-row edit over all GPUs; "
+                         "cfg5: 64 pictures split over the GPUs")
     ap.add_argument("--pictures", type=int, default=64, help="cfg5: pictures in the job")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    out = run_reference(args) if args.impl == "reference" else run_exn(args)
+    if args.impl == "reference":
+        out = run_reference(args)
+    elif args.workload == "cfg4":
+        out = run_edit(args)
+    else:
+        out = run_exn(args)
     if out is not None:
         print(json.dumps(out), flush=True)
+    try:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
+    except Exception:
+        pass
 
 
 if __name__ == "__main__":
