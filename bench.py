@@ -311,7 +311,7 @@ def run_exn(args):
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
         e2e_ms = max_over_ranks(dist, e2e_ms)
     # kernel-class times from CUDA events on the library's stream (one more picture, timed apart)
-    prof = dict(gemm_ms=0.0, attn_ms=0.0, other_ms=0.0)
+    prof = dict(gemm_ms=0.0, attn_ms=0.0, other_ms=0.0, gateup_ms=0.0)
     if not args.no_profile:
         d.profile(True)
         with torch.cuda.stream(stream):
@@ -330,6 +330,10 @@ def run_exn(args):
     total_units = args.pictures if args.workload == "cfg5" else world * B
     value = total_units * 1e3 / ms
     gemm_tflops = gf / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] else None
+    npic = len(groups[0])
+    rows_pic = (P + H * WW) + 7 * H * WW                 # rows through the block GEMMs in one picture
+    gu_flops = npic * 2.0 * rows_pic * 2 * FFN * W * args.layers
+    gu_tflops = gu_flops / (prof["gateup_ms"] * 1e-3) / 1e12 if prof["gateup_ms"] else None
     attn_tflops = af / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] else None
     ctx_bytes = total_units * P * CTX * 4       # whole job, per step
     z_bytes = total_units * LAT * H * WW * 4
@@ -359,12 +363,21 @@ def run_exn(args):
         "e2e": ({"value": round(total_units * 1e3 / e2e_ms, 4), "unit": "images/s",
                  "h2d_bytes_per_step": ctx_bytes + z_bytes, "d2h_bytes_per_step": z_bytes,
                  "ms_per_step": round(e2e_ms, 3), "finite": finite} if e2e_ms else None),
-        "roofline": {"bound": "tensor", "kernel": "k_gemm (tcgen05 GEMMs, all epilogues)",
-                     "achieved": round(gemm_tflops, 1) if gemm_tflops else None, "peak": bt, "unit": "TFLOP/s",
-                     "frac": round(gemm_tflops / bt, 4) if gemm_tflops else None, "traffic": None,
-                     "peak_source": src + " (MEASURED_PEAKS.json bf16_tflops_sustained: the GEMMs run inside a "
+        "roofline": {"bound": "tensor",
+                     "kernel": "k_gemm2<EPI_SWIGLU>: img_mlp.gate_up GEMM + SwiGLU epilogue on CTA pairs (the "
+                               "largest kernel, 32% of a picture's kernel time)",
+                     "achieved": round(gu_tflops, 1) if gu_tflops else None, "peak": bt, "unit": "TFLOP/s",
+                     "frac": round(gu_tflops / bt, 4) if gu_tflops else None,
+                     "traffic": 347.7e6,
+                     "traffic_note": "dram read+write bytes of one launch at the first step's 4224 rows (ncu, "
+                                     "profiles/gemm2_swiglu_cfg2_first_step.md); algorithmic bytes 339.7e6",
+                     "algorithmic_flop_per_launch": 2.0 * (P + H * WW) * 2 * FFN * W,
+                     "peak_source": src + " (MEASURED_PEAKS.json bf16_tflops_sustained: the kernels run inside a "
                                           "seconds-long step at the power cap; burst figure %.1f)" % bt_burst,
-                     "events": "CUDA events between kernel classes on the library's stream, one extra picture",
+                     "events": "CUDA events on the library's stream around each kernel class, one extra picture",
+                     "gateup_ms_per_picture": round(prof["gateup_ms"], 3),
+                     "all_gemms_tflops": round(gemm_tflops, 1) if gemm_tflops else None,
+                     "all_gemms_frac": round(gemm_tflops / bt, 4) if gemm_tflops else None,
                      "gemm_ms_per_picture": round(prof["gemm_ms"], 3), "attn_ms_per_picture": round(prof["attn_ms"], 3),
                      "other_ms_per_picture": round(prof["other_ms"], 3),
                      "attention_tflops": round(attn_tflops, 1) if attn_tflops else None,

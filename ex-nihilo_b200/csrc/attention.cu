@@ -11,17 +11,28 @@
 // src/cuda-dit.lisp:207-218).
 //
 // One CTA = one (sample, head) and two tiles of 128 queries (a, b) that
-// share every K/V tile:
-//   warp 0      TMA: Q_a, Q_b once; K_j, V_j (128 keys x 128 dims, bf16)
-//   warp 1      tcgen05.mma: S_x = Q_x K_j^T into TMEM, O_x += P_x V_j
-//   warps 2..5  softmax of tile a, warps 6..9 of tile b: one query row per
-//               thread straight from TMEM (32x32b loads); P_x (bf16, two per
-//               column) written back into TMEM over the first 64 columns of
-//               S_x and fed to the PV MMA from there (A operand in TMEM); O_x
-//               rescaled in TMEM only when the row maximum grows by more
-//               than 2^8
-// The MMA order PV_a(j), S_a(j+1), PV_b(j), S_b(j+1) lets one tile's softmax
-// run while the tensor core serves the other.
+// share every K/V tile.  Keys are taken 64 at a time ("units"; K and V are
+// loaded 128 keys at a time, two units a load):
+//   warp 0      TMA: Q_a, Q_b once; K_t, V_t (128 keys x 128 dims, bf16)
+//               through a ring of 4 slots
+//   warp 1, 2   tcgen05.mma for tile a, b: S_x(u) = Q_x K(u)^T (128 x 64,
+//               fp32) into one of two TMEM buffers of tile x; O_x += P_x(u)
+//               V(u) with P_x read from TMEM (A operand in TMEM)
+//   warps 3..6  softmax of tile a, warps 7..10 of tile b: one query row per
+//               thread straight from TMEM (32x32b loads); P_x(u) (bf16, two
+//               per column) written over the first 32 columns of S_x(u)'s
+//               buffer; O_x rescaled in TMEM only when the row maximum grows
+//               by more than 2^8
+// With two S buffers a tile, S_x(u+1) is already in TMEM when the softmax of
+// unit u ends, and the MMA thread computes S_x(u+2) while the softmax of u+1
+// runs: the tensor core is off the softmax's critical path.  The MMA thread
+// issues S_x(u+2) right after PV_x(u) into the buffer P_x(u) occupies; the
+// tensor core runs one thread's MMAs in order, so PV_x(u) reads P_x(u) before
+// S_x(u+2) overwrites it.
+// Each scheduler of the SM also runs two softmax warps (TMEM lane quarter q
+// is reachable only from warps w with w % 4 == q), which leave an issuing
+// thread few issue slots; one MMA thread per tile, on two schedulers, halves
+// the instructions each must get through.
 #include <stdlib.h>
 
 #include "exn_device.cuh"
@@ -34,33 +45,17 @@ int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* d
 
 namespace {
 
-constexpr int ATT_THREADS = 320;
-constexpr int TILE = 128;                 // queries per tile, keys per K/V tile
+constexpr int ATT_THREADS = 352;
+constexpr int TILE = 128;                 // queries per tile, keys per K/V load
+constexpr int UNIT = 64;                  // keys per S tile
 constexpr int HALF = TILE * 128;          // bytes of one 64-column swizzled half of a 128 x 128 bf16 tile
 constexpr int TILE_BYTES = 2 * HALF;      // 32 KB
-// K_0 V_0 K_1 V_1 ... stream through a ring of 4 tile slots, so each load has
-// a slot free well before its MMA needs it.
-constexpr int SLOTS = 4;
+constexpr int SLOTS = 4;                  // K_0 V_0 K_1 V_1 ... stream through 4 slots
 constexpr int OFF_QA = 0, OFF_QB = TILE_BYTES, OFF_SLOT = 2 * TILE_BYTES, OFF_BAR = (2 + SLOTS) * TILE_BYTES;
 constexpr int ATT_SMEM = OFF_BAR + 256 + 1024;
-constexpr uint32_t IDESC_S = idesc_bf16(128, 128);
+constexpr uint32_t IDESC_S = idesc_bf16(128, UNIT);
 constexpr uint32_t IDESC_PV = idesc_bf16(128, 128, false, true);  // V is MN-major (dims contiguous)
 constexpr float RESCALE_THRESHOLD = 8.0f;                          // log2 units
-
-// 2^x on the FMA and integer pipes, for x <= 8: Cody-Waite split x = n + f,
-// n = round(x) by the 1.5 * 2^23 magic add, f in [-1/2, 1/2]; 2^f by a
-// degree-3 polynomial fitted to 2^f on that interval (Lawson-weighted least
-// squares, max relative error 7.5e-5, far under bf16's 2^-9 rounding of P);
-// 2^n added into the exponent field; below 2^-126 (masked keys) exactly 0.
-// The MUFU pipe gives 16 ex2 a clock per SM; computing a share of each row
-// here lets the FMA pipes carry part of the softmax's exponentials.
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -126.f);
-  const float t = __fadd_rn(xc, 12582912.f);
-  const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.f));
-  const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.24261114f), f, 0.69326097f), f, 0.99992806f);
-  return x > -126.f ? __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23)) : 0.f;
-}
 
 __device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
   return g >= p ? l - 1 : (g >= b0 && g < b1 ? b1 - 1 : g);
@@ -68,15 +63,16 @@ __device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
 
 struct Bars {
   uint64_t q_full, slot_full[SLOTS], slot_empty[SLOTS];
-  uint64_t s_full[2], p_full[2], o_full[2];
-  uint64_t done;
+  uint64_t s_full[2][2], p_full[2][2];  // [tile][S buffer]
+  uint64_t pv_done[2];                  // one phase per PV_x(u); waited only with at most one PV in flight
+  uint64_t o_full[2];                   // after the last PV_x
+  uint64_t done[2];
   uint32_t tmem_slot;
   int abort_flag;
 };
 
 }  // namespace
 
-template <int POLY>  // of each 8 exponentials of a row, POLY are computed by exp2_fma
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
@@ -90,20 +86,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int qt = blockIdx.x, head = blockIdx.y, sample = blockIdx.z;
   const int qlast = min(nq, (qt + 1) * 2 * TILE) - 1;
   const int last_key = xa_lim(q0 + qlast, p, l, b0, b1);
-  const int nkv = last_key / TILE + 1;
+  const int nunits = last_key / UNIT + 1;   // 64-key units any row of the CTA sees
+  const int nloads = (nunits + 1) / 2;      // 128-key K/V loads
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int i = 0; i < SLOTS; ++i) {
       mbar_init(&bars->slot_full[i], 1);
-      mbar_init(&bars->slot_empty[i], 1);
+      mbar_init(&bars->slot_empty[i], 2);  // a K or V tile is free once both tiles' MMAs are done with it
     }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars->s_full[x], 1);
-      mbar_init(&bars->p_full[x], 4);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&bars->s_full[x][b], 1);
+        mbar_init(&bars->p_full[x][b], 4);  // one arrival per softmax warp
+      }
+      mbar_init(&bars->pv_done[x], 1);
       mbar_init(&bars->o_full[x], 1);
+      mbar_init(&bars->done[x], 1);
     }
-    mbar_init(&bars->done, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
-  // TMEM columns: S_a [0,128), S_b [128,256), O_a [256,384), O_b [384,512)
+  // TMEM columns: S_a buffers [0,64) [64,128), S_b [128,192) [192,256), O_a [256,384), O_b [384,512)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -128,9 +128,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int hf = 0; hf < 2; ++hf)
           tma_load_3d(smem + (x ? OFF_QB : OFF_QA) + hf * HALF, &tmQ, &bars->q_full, hx + hf * 64,
                       qt * 2 * TILE + x * TILE, sample);
-      // load number t: K_{t/2} for even t, V_{t/2} for odd t; slot t % 3, its (t / 3)-th use
+      // load number t: K_{t/2} for even t, V_{t/2} for odd t; slot t % SLOTS, its (t / SLOTS)-th use
       int issued = 0;
-      for (int t = 0; t < 2 * nkv; ++t) {
+      for (int t = 0; t < 2 * nloads; ++t) {
         const int slot = t % SLOTS;
         const uint32_t use = static_cast<uint32_t>(t / SLOTS);
         if (!mbar_wait(&bars->slot_empty[slot], (use & 1) ^ 1, abort_flag, status, STATUS_TIMEOUT_ATTN)) break;
@@ -148,78 +148,76 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           mbar_wait(&bars->slot_full[t % SLOTS], static_cast<uint32_t>(t / SLOTS) & 1, &no_abort, nullptr, 0);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp <= 2) {
     if (lane == 0) {
-      // descriptors formed once; start addresses then advance in 16-byte units
-      const uint64_t dq_a = sdesc_sw128(smem_u32(smem + OFF_QA), 16, 1024);
-      const uint64_t dq_b = sdesc_sw128(smem_u32(smem + OFF_QB), 16, 1024);
-      const uint64_t dk0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), 16, 1024);     // keys x dims, K-major
-      const uint64_t dv0 = sdesc_sw128(smem_u32(smem + OFF_SLOT), HALF, 1024);   // keys x dims read MN-major
-      const uint32_t slot0 = smem_u32(smem + OFF_SLOT);
-      auto issue_s = [&](uint64_t dq, uint32_t k_addr, uint32_t d) {
-        const uint64_t dk = dk0 + static_cast<uint64_t>((k_addr - slot0) >> 4);
+      // ---- the MMAs of tile x.  This thread shares its scheduler with two busy softmax warps, so
+      // its instruction stream is kept short: descriptors are formed once, as 32-bit low words
+      // over a common high word (every operand here is 128B-swizzled with 1024-byte 8-row
+      // groups), and each MMA then costs a constant add per operand.
+      const int x = warp - 1;
+      const uint32_t dhi = static_cast<uint32_t>(sdesc_sw128(0, 16, 1024) >> 32);
+      const uint32_t qlo = static_cast<uint32_t>(sdesc_sw128(smem_u32(smem + (x ? OFF_QB : OFF_QA)), 16, 1024));
+      const uint32_t klo = static_cast<uint32_t>(sdesc_sw128(smem_u32(smem + OFF_SLOT), 16, 1024));    // K-major
+      const uint32_t vlo = static_cast<uint32_t>(sdesc_sw128(smem_u32(smem + OFF_SLOT), HALF, 1024));  // MN-major
+      const uint32_t s_tm = tmem + x * 128, o_tm = tmem + 256 + x * 128;
+      // S_x(u) = Q_x K(u)^T: keys (u % 2) * 64 .. +63 of load 2 * (u / 2), into S buffer u % 2
+      auto issue_s = [&](int u) {
+        const uint32_t k = klo + ((((u >> 1) * 2) % SLOTS) * TILE_BYTES + (u & 1) * UNIT * 128) / 16;
+        const uint32_t d = s_tm + (u & 1) * UNIT;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t o = static_cast<uint64_t>(((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
-          umma_ss(d, dq + o, dk + o, IDESC_S, kk ? 1u : 0u);
+          const uint32_t o = ((kk >> 2) * HALF + (kk & 3) * 32) / 16;
+          umma_ss_lo(d, qlo + o, k + o, dhi, IDESC_S, kk ? 1u : 0u);
         }
       };
-      // O_x += P_x V: P_x in TMEM at S_x's columns (8 columns = 16 keys per instruction)
-      auto issue_pv = [&](uint32_t p_tmem, uint32_t v_addr, uint32_t d, bool acc) {
-        const uint64_t dv = dv0 + static_cast<uint64_t>((v_addr - slot0) >> 4);
+      // O_x += P_x(u) V(u): P_x in TMEM at S buffer u % 2 (8 columns = 16 keys per instruction)
+      auto issue_pv = [&](int u) {
+        const uint32_t v = vlo + ((((u >> 1) * 2 + 1) % SLOTS) * TILE_BYTES + (u & 1) * UNIT * 128) / 16;
+        const uint32_t a = s_tm + (u & 1) * UNIT;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(d, p_tmem + kk * 8, dv + static_cast<uint64_t>((kk * 2048) >> 4), IDESC_PV, (acc || kk) ? 1u : 0u);
+        for (int kk = 0; kk < UNIT / 16; ++kk)
+          umma_ts_lo(o_tm, a + kk * 8, v + kk * 2048 / 16, dhi, IDESC_PV, (u > 0 || kk) ? 1u : 0u);
       };
-      // wait for load T (K_{T/2} or V_{T/2}); its slot's address
-      auto wait_load = [&](int t, uint32_t& addr) -> bool {
-        const int slot = t % SLOTS;
-        addr = slot0 + slot * TILE_BYTES;
-        return mbar_wait(&bars->slot_full[slot], static_cast<uint32_t>(t / SLOTS) & 1, abort_flag, status,
+      auto wait_load = [&](int t) {
+        return mbar_wait(&bars->slot_full[t % SLOTS], static_cast<uint32_t>(t / SLOTS) & 1, abort_flag, status,
                          STATUS_TIMEOUT_ATTN);
       };
-      uint32_t k_addr = 0, v_addr = 0;
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) && wait_load(0, k_addr);
+      bool ok = mbar_wait(&bars->q_full, 0, abort_flag, status, STATUS_TIMEOUT_ATTN) && wait_load(0);
       if (ok) {
         tc_fence_after();
-        issue_s(dq_a, k_addr, tmem + 0);
-        umma_commit(&bars->s_full[0]);
-        issue_s(dq_b, k_addr, tmem + 128);
-        umma_commit(&bars->s_full[1]);
-        umma_commit(&bars->slot_empty[0]);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const uint32_t par = j & 1;
-        const bool more = j + 1 < nkv;
-        if (!(ok = wait_load(2 * j + 1, v_addr))) break;
-        if (!(ok = mbar_wait(&bars->p_full[0], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
-        tc_fence_after();
-        issue_pv(tmem + 0, v_addr, tmem + 256, j > 0);
-        if (!more) umma_commit(&bars->o_full[0]);
-        if (more) {
-          if (!(ok = wait_load(2 * j + 2, k_addr))) break;
-          tc_fence_after();
-          issue_s(dq_a, k_addr, tmem + 0);
-          umma_commit(&bars->s_full[0]);
+        for (int u = 0; u < 2 && u < nunits; ++u) {
+          issue_s(u);
+          umma_commit(&bars->s_full[x][u]);
         }
-        if (!(ok = mbar_wait(&bars->p_full[1], par, abort_flag, status, STATUS_TIMEOUT_ATTN))) break;
-        tc_fence_after();
-        issue_pv(tmem + 128, v_addr, tmem + 384, j > 0);
-        umma_commit(&bars->slot_empty[(2 * j + 1) % SLOTS]);
-        if (!more) umma_commit(&bars->o_full[1]);
-        if (more) {
-          issue_s(dq_b, k_addr, tmem + 128);
-          umma_commit(&bars->s_full[1]);
-          umma_commit(&bars->slot_empty[(2 * j + 2) % SLOTS]);
-        }
+        umma_commit(&bars->slot_empty[0]);  // K_0: both its units issued
       }
-      umma_commit(&bars->done);
+      for (int u = 0; u < nunits && ok; ++u) {
+        const int b = u & 1;
+        const bool more = u + 2 < nunits;
+        if (b == 0 && !(ok = wait_load(2 * (u >> 1) + 1))) break;  // V(u)
+        if (!(ok = mbar_wait(&bars->p_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
+                             STATUS_TIMEOUT_ATTN)))
+          break;
+        tc_fence_after();
+        issue_pv(u);
+        umma_commit(&bars->pv_done[x]);
+        if (u + 1 == nunits) umma_commit(&bars->o_full[x]);
+        if (more) {
+          if (b == 0 && !(ok = wait_load(2 * ((u + 2) >> 1)))) break;  // K(u + 2)
+          issue_s(u + 2);
+          umma_commit(&bars->s_full[x][b]);
+        }
+        // this tile's share of freeing the slots whose last reader was just issued
+        if (b == 1 || u + 1 == nunits) umma_commit(&bars->slot_empty[(2 * (u >> 1) + 1) % SLOTS]);   // V(u)
+        if (more && (b == 1 || u + 3 == nunits)) umma_commit(&bars->slot_empty[(2 * ((u + 2) >> 1)) % SLOTS]);
+      }
+      umma_commit(&bars->done[x]);  // every MMA queued above has finished before TMEM is released
       volatile int no_abort = 0;
-      mbar_wait(&bars->done, 0, &no_abort, nullptr, 0);
+      mbar_wait(&bars->done[x], 0, &no_abort, nullptr, 0);
     }
   } else {
     // ---- softmax: tile x, TMEM lane quarter wq, query row r of the tile
-    const int x = (warp - 2) >> 2;
+    const int x = (warp - 3) >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const int qi = qt * 2 * TILE + x * TILE + r;  // query index within the pass
@@ -229,35 +227,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const uint32_t o_addr = tmem + lane_off + 256 + x * 128;
     float m = -INFINITY, lsum = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait_warp(&bars->s_full[x], j & 1, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
+    const uint64_t sc2 = f2(scale_log2, scale_log2);
+    for (int u = 0; u < nunits; ++u) {
+      const int b = u & 1;
+      if (!mbar_wait_warp(&bars->s_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
+                          STATUS_TIMEOUT_ATTN)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[128];
+      float s[UNIT];
       {
-        uint32_t rr[128];
-        tmem_ld128(s_addr, rr);
+        uint32_t rr[UNIT];
+        tmem_ld64(s_addr + b * UNIT, rr);
 #pragma unroll
-        for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(rr[i]);
+        for (int i = 0; i < UNIT; ++i) s[i] = __uint_as_float(rr[i]);
       }
-      const int key0 = j * TILE;
-      if (key0 + TILE - 1 > lim) {
+      const int key0 = u * UNIT;
+      if (key0 + UNIT - 1 > lim) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 0; c < UNIT; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
       }
-      // row maximum as an 8-way tree (a serial chain of 128 would cost its latency every tile)
+      // row maximum: 8 independent chains of 3-input maxima, then a tree
       float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+      for (int i = 0; i < 8; ++i) m8[i] = fmax3(s[i], s[8 + i], s[16 + i]);
 #pragma unroll
-      for (int c = 8; c < 128; c += 8)
+      for (int c = 24; c < UNIT - 8; c += 16)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[UNIT - 8 + i]);
+      const float mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = m_new > m + RESCALE_THRESHOLD;
       float alpha = 1.f;
@@ -266,7 +268,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         lsum *= alpha;
         m = m_new;
       }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
+      if (u > 0 && __any_sync(0xffffffffu, need)) {
+        // O_x holds the sum through PV_x(u-1): wait for it, then scale in place.  PV_x(u-2) has
+        // finished (it was queued before S_x(u), whose commit this softmax waited for), so the
+        // parity of u-1 is unambiguous.
+        if (!mbar_wait_warp(&bars->pv_done[x], static_cast<uint32_t>(u - 1) & 1, abort_flag, status,
+                            STATUS_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t rr[32];
@@ -277,35 +288,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         tmem_st_wait();
       }
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[64];  // P as bf16 pairs: key 2c and 2c+1 in column c
+      // x = s * scale - m and the row sums on paired f32 instructions (two keys per issue)
+      const uint64_t nm2 = f2(-m, -m);
+      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
+      uint32_t pk[UNIT / 2];  // P as bf16 pairs: key 2c and 2c+1 in column c
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        float e[8];
+      for (int c8 = 0; c8 < UNIT / 8; ++c8) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xv = fmaf(s[c16 * 8 + i], scale_log2, -m);
-          e[i] = i >= 8 - POLY ? exp2_fma(xv) : fast_exp2(xv);
-          ps8[i] += e[i];
+        for (int i = 0; i < 4; ++i) {
+          float x0, x1;
+          f2_split(ffma2(f2(s[c8 * 8 + 2 * i], s[c8 * 8 + 2 * i + 1]), sc2, nm2), x0, x1);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+          ps2[i] = fadd2(ps2[i], f2(e0, e1));
+          pk[c8 * 4 + i] = pack_bf16x2(e0, e1);
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) pk[c16 * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
       }
-      lsum += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       {
-        uint32_t half0[32], half1[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          half0[i] = pk[i];
-          half1[i] = pk[32 + i];
-        }
-        tmem_st32(s_addr, half0);
-        tmem_st32(s_addr + 32, half1);
-        tmem_st_wait();
+        float a0, a1;
+        f2_split(fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3])), a0, a1);
+        lsum += a0 + a1;
       }
+      tmem_st32(s_addr + b * UNIT, pk);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[x]);
+      if (lane == 0) mbar_arrive(&bars->p_full[x][b]);
     }
     if (ok && mbar_wait_warp(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
       tc_fence_after();
@@ -339,16 +346,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   if (a.nq <= 0 || a.l <= 0 || a.width % 128 || a.heads * 128 != a.width || a.kv_rows < a.l) return -1;
   if (a.q0 + a.nq > a.l) return -1;
-  static int poly = -1;  // EXN_ATTN_POLY: exponentials of each 8 on the FMA pipes (0, 1, 2 or 3)
-  if (poly < 0) {
-    const char* e = getenv("EXN_ATTN_POLY");
-    const int v = e ? atoi(e) : 0;
-    if (cudaFuncSetAttribute(k_attention<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attention<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attention<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attention<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
       return -3;
-    poly = v < 0 || v > 3 ? 0 : v;
+    attr_set = true;
   }
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, TILE, 1};
@@ -361,9 +363,8 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
   dim3 grid((a.nq + 2 * TILE - 1) / (2 * TILE), a.heads, a.batch);
-  auto kern = poly == 0 ? k_attention<0> : poly == 1 ? k_attention<1> : poly == 2 ? k_attention<2> : k_attention<3>;
-  kern<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
-                                            a.scale_log2, d_status);
+  k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
+                                                   a.scale_log2, d_status);
   return static_cast<int>(cudaGetLastError());
 }
 

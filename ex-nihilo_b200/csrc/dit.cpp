@@ -205,7 +205,7 @@ struct exn_handle {
   float* trace_host = nullptr;
   size_t trace_floats = 0;
   Profile prof;
-  double last_ms[3] = {0, 0, 0};
+  double last_ms[4] = {0, 0, 0, 0};  // GEMM (other than gate_up), attention, other, gate_up GEMM
   long long launches = 0;  // kernels of this library queued by the step code since open
 
   // sequence parallelism over `world` handles (one per GPU)
@@ -515,7 +515,7 @@ void prof_mark(exn_handle* h, int cat) {
 void prof_collect(exn_handle* h) {
   if (!h->prof.on || h->prof.marks.size() < 2) return;
   cudaEventSynchronize(h->prof.marks.back().first);
-  double acc[3] = {0, 0, 0};
+  double acc[4] = {0, 0, 0, 0};
   for (size_t i = 0; i + 1 < h->prof.marks.size(); ++i) {
     float ms = 0;
     cudaEventElapsedTime(&ms, h->prof.marks[i].first, h->prof.marks[i + 1].first);
@@ -523,7 +523,7 @@ void prof_collect(exn_handle* h) {
   }
   for (auto& m : h->prof.marks) cudaEventDestroy(m.first);
   h->prof.marks.clear();
-  for (int i = 0; i < 3; ++i) h->last_ms[i] = acc[i];
+  for (int i = 0; i < 4; ++i) h->last_ms[i] = acc[i];
 }
 
 // ---------------------------------------------------------------------------- one step
@@ -690,13 +690,14 @@ int run_step(exn_handle* h, const StepIn& in) {
       return rc;
     prof_mark(h, 2);
     ln_mod_launch(h->x, h->y, h->modv + 2 * W, 4 * W, rows, W, n, n, 0, n0, p, 0, h->st);
-    prof_mark(h, 0);
+    prof_mark(h, 3);
     GemmEpi eg;
     eg.out = h->ff;
     eg.ld_out = c.ffn;
     if ((rc = gemm(h, h->y, W, h->w_gu + static_cast<size_t>(il) * 2 * c.ffn * W, W, rows, 2 * c.ffn, W, EPI_SWIGLU,
                    eg)))
       return rc;
+    prof_mark(h, 0);
     GemmEpi ed = eo;
     ed.mod = h->modv + 3 * W;
     if ((rc = gemm(h, h->ff, c.ffn, h->w_down + static_cast<size_t>(il) * W * c.ffn, c.ffn, rows, W, c.ffn,
@@ -1694,11 +1695,12 @@ int exn_test_profile(exn_handle* h, int on) {
 
 long long exn_test_launch_count(const exn_handle* h) { return h ? h->launches : -1; }
 
-int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms) {
+int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms, double* gateup_ms) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_last_profile: null handle");
-  if (gemm_ms) *gemm_ms = h->last_ms[0];
+  if (gemm_ms) *gemm_ms = h->last_ms[0] + h->last_ms[3];
   if (attn_ms) *attn_ms = h->last_ms[1];
   if (other_ms) *other_ms = h->last_ms[2];
+  if (gateup_ms) *gateup_ms = h->last_ms[3];
   return EXN_OK;
 }
 

@@ -102,7 +102,7 @@ def lib():
         "exn_test_weight_bf16": (ctypes.c_int, [H, ctypes.c_char_p, vp, ctypes.c_size_t]),
         "exn_test_synth_normal": (ctypes.c_int, [H, vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
                                                  ctypes.c_double]),
-        "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 3),
+        "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 4),
         "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_launch_count": (ctypes.c_longlong, [H]),
     }
@@ -272,9 +272,9 @@ class Dit:
         self._ck(lib().exn_test_profile(self.h, 1 if on else 0))
 
     def last_profile(self):
-        g, a, o = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
-        self._ck(lib().exn_test_last_profile(self.h, ctypes.byref(g), ctypes.byref(a), ctypes.byref(o)))
-        return dict(gemm_ms=g.value, attn_ms=a.value, other_ms=o.value)
+        g, a, o, u = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        self._ck(lib().exn_test_last_profile(self.h, ctypes.byref(g), ctypes.byref(a), ctypes.byref(o), ctypes.byref(u)))
+        return dict(gemm_ms=g.value, attn_ms=a.value, other_ms=o.value, gateup_ms=u.value)
 
     def launch_count(self):
         return int(lib().exn_test_launch_count(self.h))

@@ -55,8 +55,9 @@ int exn_test_profile(exn_handle* h, int on);
 long long exn_test_launch_count(const exn_handle* h);
 
 /* Kernel time of the last exn_generate* / exn_velocity call in ms per
- * category (gemm, attention, other) when timing is on, else zeros. */
-int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms);
+ * category when timing is on, else zeros: every GEMM, attention, the rest,
+ * and of the GEMMs the gate_up + SwiGLU ones alone. */
+int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms, double* gateup_ms);
 
 #ifdef __cplusplus
 }
