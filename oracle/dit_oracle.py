@@ -197,10 +197,14 @@ class SynthWeights:
     vec: dict = field(default_factory=dict)    # name -> fp32 (n,)
 
     @classmethod
-    def make(cls, shape: Shape, seed: int = 1):
+    def make(cls, shape: Shape, seed: int = 1, only=None):
+        """ONLY, a predicate on tensor names, restricts the set made (each
+        tensor's values depend on its index in the full list, not on the set)."""
         sw = cls(shape, seed)
         std = synth_std(shape.width)
         for i, (name, dims) in enumerate(expected_tensors(shape)):
+            if only is not None and not only(name):
+                continue
             v = synth_tensor_f32(seed, i, name, dims, std)
             if len(dims) == 1:
                 sw.vec[name] = v
@@ -335,13 +339,34 @@ def modulation(wt, sh: Shape, sigma):
     return emb, pieces, sc
 
 
+def block(wt, sh: Shape, il, x, pieces, row, cos, sin, p, b0=0, b1=0):
+    """Block IL on the sequence X (ref_dit.py:133-146): PIECES = the
+    modulation rows (scale1, gate1, scale2, gate2), ROW the modulation row of
+    each sequence row (0 image, 1 prefix), COS/SIN its RoPE tables."""
+    W, HD, heads = sh.width, sh.head_dim, sh.heads
+    scale1, gate1, scale2, gate2 = pieces
+    n = x.shape[0]
+    b = "transformer_blocks.%d." % il
+    y = layernorm(x) * (1.0 + scale1[row])
+    q = linear(y, wt(b + "attn.to_q.weight")).reshape(n, heads, HD)
+    k = linear(y, wt(b + "attn.to_k.weight")).reshape(n, heads, HD)
+    v = linear(y, wt(b + "attn.to_v.weight")).reshape(n, heads, HD)
+    q = rope(rmsnorm(q, wt(b + "attn.norm_q.weight")), cos, sin)
+    k = rope(rmsnorm(k, wt(b + "attn.norm_k.weight")), cos, sin)
+    att = attention(q, k, v, 0, p, n, b0, b1).reshape(n, W)
+    x = x + np.tanh(gate1[row]) * linear(att, wt(b + "attn.to_out.0.weight"))
+    y = layernorm(x) * (1.0 + scale2[row])
+    gu = linear(y, wt(b + "img_mlp.gate_up.weight"))
+    y = silu(gu[:, :sh.ffn]) * gu[:, sh.ffn:]
+    x = x + np.tanh(gate2[row]) * linear(y, wt(b + "img_mlp.out.weight"))
+    return x.astype(np.float32)
+
+
 def forward(wt, sh: Shape, ctx, latent, sigma, ref=None, trace=None):
     """The velocity (64 x H x W) at SIGMA: ref_dit.py:108-153, with the edit
     reference of src/cuda-dit.lisp:137-192 when REF = (A, ref_latent 64 x RH x
     RW): the reference picture's rows go into the prefix after text row A.
     TRACE, a list, receives txt_in's output and x after every block."""
-    W, HD = sh.width, sh.head_dim
-    heads = sh.heads
     ptext = ctx.shape[0]
     c, h, w = latent.shape
     _, (scale1, gate1, scale2, gate2), sc = modulation(wt, sh, sigma)
@@ -363,20 +388,7 @@ def forward(wt, sh: Shape, ctx, latent, sigma, ref=None, trace=None):
     row = np.where(np.arange(n) < p, 1, 0)
     cos, sin = rope_tables(dit_positions(p, h, w, refpos))
     for il in range(sh.layers):
-        b = "transformer_blocks.%d." % il
-        y = layernorm(x) * (1.0 + scale1[row])
-        q = linear(y, wt(b + "attn.to_q.weight")).reshape(n, heads, HD)
-        k = linear(y, wt(b + "attn.to_k.weight")).reshape(n, heads, HD)
-        v = linear(y, wt(b + "attn.to_v.weight")).reshape(n, heads, HD)
-        q = rope(rmsnorm(q, wt(b + "attn.norm_q.weight")), cos, sin)
-        k = rope(rmsnorm(k, wt(b + "attn.norm_k.weight")), cos, sin)
-        att = attention(q, k, v, 0, p, n, b0, b1).reshape(n, W)
-        x = x + np.tanh(gate1[row]) * linear(att, wt(b + "attn.to_out.0.weight"))
-        y = layernorm(x) * (1.0 + scale2[row])
-        gu = linear(y, wt(b + "img_mlp.gate_up.weight"))
-        y = silu(gu[:, :sh.ffn]) * gu[:, sh.ffn:]
-        x = x + np.tanh(gate2[row]) * linear(y, wt(b + "img_mlp.out.weight"))
-        x = x.astype(np.float32)
+        x = block(wt, sh, il, x, (scale1, gate1, scale2, gate2), row, cos, sin, p, b0, b1)
         if trace is not None:
             trace.append(x)
     x = x[p:]
