@@ -230,8 +230,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const uint64_t sc2 = f2(scale_log2, scale_log2);
     for (int u = 0; u < nunits; ++u) {
       const int b = u & 1;
-      if (!mbar_wait_warp(&bars->s_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
-                          STATUS_TIMEOUT_ATTN)) {
+      // the warp stays converged through the whole loop (warp-uniform waits and branches), so
+      // the TMEM loads and stores need no __syncwarp
+      if (!mbar_wait_uniform(&bars->s_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
+                             STATUS_TIMEOUT_ATTN)) {
         ok = false;
         break;
       }
@@ -239,12 +241,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       float s[UNIT];
       {
         uint32_t rr[UNIT];
-        tmem_ld64(s_addr + b * UNIT, rr);
+        tmem_ld64_conv(s_addr + b * UNIT, rr);
 #pragma unroll
         for (int i = 0; i < UNIT; ++i) s[i] = __uint_as_float(rr[i]);
       }
       const int key0 = u * UNIT;
-      if (key0 + UNIT - 1 > lim) {
+      if (__any_sync(0xffffffffu, key0 + UNIT - 1 > lim)) {
 #pragma unroll
         for (int c = 0; c < UNIT; ++c)
           if (key0 + c > lim) s[c] = -INFINITY;
@@ -262,18 +264,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const float mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
       const float m_new = fmaxf(m, mx * scale_log2);
       const bool need = m_new > m + RESCALE_THRESHOLD;
-      float alpha = 1.f;
-      if (need) {
-        alpha = fast_exp2(m - m_new);
-        lsum *= alpha;
-        m = m_new;
-      }
+      const float alpha = need ? fast_exp2(m - m_new) : 1.f;
+      lsum *= alpha;
+      m = need ? m_new : m;
       if (u > 0 && __any_sync(0xffffffffu, need)) {
         // O_x holds the sum through PV_x(u-1): wait for it, then scale in place.  PV_x(u-2) has
         // finished (it was queued before S_x(u), whose commit this softmax waited for), so the
         // parity of u-1 is unambiguous.
-        if (!mbar_wait_warp(&bars->pv_done[x], static_cast<uint32_t>(u - 1) & 1, abort_flag, status,
-                            STATUS_TIMEOUT_ATTN)) {
+        if (!mbar_wait_uniform(&bars->pv_done[x], static_cast<uint32_t>(u - 1) & 1, abort_flag, status,
+                               STATUS_TIMEOUT_ATTN)) {
           ok = false;
           break;
         }
@@ -308,13 +307,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         f2_split(fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3])), a0, a1);
         lsum += a0 + a1;
       }
-      tmem_st32(s_addr + b * UNIT, pk);
+      tmem_st32_conv(s_addr + b * UNIT, pk);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[x][b]);
     }
-    if (ok && mbar_wait_warp(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
+    if (ok && mbar_wait_uniform(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
       tc_fence_after();
       const float inv = 1.f / lsum;
       bf16* dst = out + (static_cast<long long>(sample) * nq + qi) * width + head * 128;

@@ -111,6 +111,27 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return ok != 0;
 }
 
+// The same wait taken by every lane of a converged warp, which stays converged
+// throughout: each poll and each give-up test is one warp vote, so there is
+// no single-lane branch for the scheduler to resolve.
+__device__ __forceinline__ bool mbar_wait_uniform(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* status, int code) {
+  if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (__any_sync(0xffffffffu, mbar_try_wait_sleep(bar, parity, 100000u))) return true;
+    const bool aborted = __any_sync(0xffffffffu, *abort_flag != 0);
+    if (aborted) return false;
+    if (__any_sync(0xffffffffu, globaltimer() - t0 > EXN_WAIT_NS)) {
+      if ((threadIdx.x & 31) == 0) {
+        *abort_flag = 1;
+        if (status) atomicOr(status, code);
+      }
+      return false;
+    }
+  }
+}
+
 // One lane of a converged warp, chosen by the hardware (elect.sync).  Loops
 // that issue TMA copies and MMAs run on the whole warp so the addresses and
 // descriptors they compute stay warp-uniform; only the issue is single-lane.
@@ -287,6 +308,17 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
                : EXN_U8(0), EXN_U8(8), EXN_U8(16), EXN_U8(24), EXN_U8(32), EXN_U8(40), EXN_U8(48), EXN_U8(56)::"memory");
 }
 
+// The same for a warp known to be converged (no __syncwarp before the load)
+__device__ __forceinline__ void tmem_ld64_conv(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : EXN_R8(0), EXN_R8(8), EXN_R8(16), EXN_R8(24), EXN_R8(32), EXN_R8(40), EXN_R8(48), EXN_R8(56)
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : EXN_U8(0), EXN_U8(8), EXN_U8(16), EXN_U8(24), EXN_U8(32), EXN_U8(40), EXN_U8(48), EXN_U8(56)::"memory");
+}
+
 // 32 lanes x 128 columns in one instruction; the wait ties all 128 registers.
 __device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
   __syncwarp();
@@ -299,6 +331,15 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      EXN_S8(0), EXN_S8(8), EXN_S8(16), EXN_S8(24)
+      : "memory");
+}
+
+// The same for a warp known to be converged
+__device__ __forceinline__ void tmem_st32_conv(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
       "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
