@@ -228,90 +228,101 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     float m = -INFINITY, lsum = 0.f;
     bool ok = true;
     const uint64_t sc2 = f2(scale_log2, scale_log2);
+    // Ping-pong: this warp and the other tile's warp on the same scheduler (same lane quarter)
+    // take turns with their exponentials, a then b, through two 64-thread named barriers.  Each
+    // exp phase then has the scheduler's MUFU pipe to itself, and the two tiles stay half a unit
+    // apart, so one tile's MMAs run during the other's softmax.  Every warp takes every
+    // iteration and every turn, also after a failed wait (then with the work skipped), so no
+    // partner is left waiting at a barrier.
+    const uint32_t my_turn = (x ? 5u : 1u) + static_cast<uint32_t>(wq);
+    const uint32_t other_turn = (x ? 1u : 5u) + static_cast<uint32_t>(wq);
+    if (x == 1) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");  // tile a goes first
     for (int u = 0; u < nunits; ++u) {
       const int b = u & 1;
       // the warp stays converged through the whole loop (warp-uniform waits and branches), so
       // the TMEM loads and stores need no __syncwarp
-      if (!mbar_wait_uniform(&bars->s_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
-                             STATUS_TIMEOUT_ATTN)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+      ok = ok && mbar_wait_uniform(&bars->s_full[x][b], static_cast<uint32_t>(u >> 1) & 1, abort_flag, status,
+                                   STATUS_TIMEOUT_ATTN);
       float s[UNIT];
-      {
-        uint32_t rr[UNIT];
-        tmem_ld64_conv(s_addr + b * UNIT, rr);
-#pragma unroll
-        for (int i = 0; i < UNIT; ++i) s[i] = __uint_as_float(rr[i]);
-      }
-      const int key0 = u * UNIT;
-      if (__any_sync(0xffffffffu, key0 + UNIT - 1 > lim)) {
-#pragma unroll
-        for (int c = 0; c < UNIT; ++c)
-          if (key0 + c > lim) s[c] = -INFINITY;
-      }
-      // row maximum: 8 independent chains of 3-input maxima, then a tree
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = fmax3(s[i], s[8 + i], s[16 + i]);
-#pragma unroll
-      for (int c = 24; c < UNIT - 8; c += 16)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], s[c + i], s[c + 8 + i]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[UNIT - 8 + i]);
-      const float mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const bool need = m_new > m + RESCALE_THRESHOLD;
-      const float alpha = need ? fast_exp2(m - m_new) : 1.f;
-      lsum *= alpha;
-      m = need ? m_new : m;
-      if (u > 0 && __any_sync(0xffffffffu, need)) {
-        // O_x holds the sum through PV_x(u-1): wait for it, then scale in place.  PV_x(u-2) has
-        // finished (it was queued before S_x(u), whose commit this softmax waited for), so the
-        // parity of u-1 is unambiguous.
-        if (!mbar_wait_uniform(&bars->pv_done[x], static_cast<uint32_t>(u - 1) & 1, abort_flag, status,
-                               STATUS_TIMEOUT_ATTN)) {
-          ok = false;
-          break;
-        }
+      if (ok) {
         tc_fence_after();
+        {
+          uint32_t rr[UNIT];
+          tmem_ld64_conv(s_addr + b * UNIT, rr);
+#pragma unroll
+          for (int i = 0; i < UNIT; ++i) s[i] = __uint_as_float(rr[i]);
+        }
+        const int key0 = u * UNIT;
+        if (__any_sync(0xffffffffu, key0 + UNIT - 1 > lim)) {
+#pragma unroll
+          for (int c = 0; c < UNIT; ++c)
+            if (key0 + c > lim) s[c] = -INFINITY;
+        }
+        // row maximum: 8 independent chains of 3-input maxima, then a tree
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmax3(s[i], s[8 + i], s[16 + i]);
+#pragma unroll
+        for (int c = 24; c < UNIT - 8; c += 16)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[UNIT - 8 + i]);
+        const float mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
+        const float m_new = fmaxf(m, mx * scale_log2);
+        const bool need = m_new > m + RESCALE_THRESHOLD;
+        const float alpha = need ? fast_exp2(m - m_new) : 1.f;
+        lsum *= alpha;
+        m = need ? m_new : m;
+        if (u > 0 && __any_sync(0xffffffffu, need)) {
+          // O_x holds the sum through PV_x(u-1): wait for it, then scale in place.  PV_x(u-2)
+          // has finished (it was queued before S_x(u), whose commit this softmax waited for), so
+          // the parity of u-1 is unambiguous.
+          ok = mbar_wait_uniform(&bars->pv_done[x], static_cast<uint32_t>(u - 1) & 1, abort_flag, status,
+                                 STATUS_TIMEOUT_ATTN);
+          if (ok) {
+            tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t rr[32];
-          tmem_ld32(o_addr + c * 32, rr);
+            for (int c = 0; c < 4; ++c) {
+              uint32_t ov[32];
+              tmem_ld32(o_addr + c * 32, ov);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-          tmem_st32(o_addr + c * 32, rr);
+              for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+              tmem_st32(o_addr + c * 32, ov);
+            }
+            tmem_st_wait();
+          }
         }
-        tmem_st_wait();
       }
-      // x = s * scale - m and the row sums on paired f32 instructions (two keys per issue)
-      const uint64_t nm2 = f2(-m, -m);
-      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
+      asm volatile("bar.sync %0, 64;" ::"r"(my_turn) : "memory");
       uint32_t pk[UNIT / 2];  // P as bf16 pairs: key 2c and 2c+1 in column c
+      if (ok) {
+        // x = s * scale - m and the row sums on paired f32 instructions (two keys per issue)
+        const uint64_t nm2 = f2(-m, -m);
+        uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-      for (int c8 = 0; c8 < UNIT / 8; ++c8) {
+        for (int c8 = 0; c8 < UNIT / 8; ++c8) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0, x1;
-          f2_split(ffma2(f2(s[c8 * 8 + 2 * i], s[c8 * 8 + 2 * i + 1]), sc2, nm2), x0, x1);
-          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
-          ps2[i] = fadd2(ps2[i], f2(e0, e1));
-          pk[c8 * 4 + i] = pack_bf16x2(e0, e1);
+          for (int i = 0; i < 4; ++i) {
+            float x0, x1;
+            f2_split(ffma2(f2(s[c8 * 8 + 2 * i], s[c8 * 8 + 2 * i + 1]), sc2, nm2), x0, x1);
+            const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+            ps2[i] = fadd2(ps2[i], f2(e0, e1));
+            pk[c8 * 4 + i] = pack_bf16x2(e0, e1);
+          }
         }
-      }
-      {
         float a0, a1;
         f2_split(fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3])), a0, a1);
         lsum += a0 + a1;
       }
-      tmem_st32_conv(s_addr + b * UNIT, pk);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[x][b]);
+      if (x == 0 || u + 1 < nunits) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");
+      if (ok) {
+        tmem_st32_conv(s_addr + b * UNIT, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[x][b]);
+      }
     }
     if (ok && mbar_wait_uniform(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
       tc_fence_after();
