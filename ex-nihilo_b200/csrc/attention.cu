@@ -61,6 +61,12 @@ __device__ __forceinline__ int xa_lim(int g, int p, int l, int b0, int b1) {
   return g >= p ? l - 1 : (g >= b0 && g < b1 ? b1 - 1 : g);
 }
 
+// Sequence-parallel output: each query row goes to the rank that keeps it (peer memory)
+struct SpOut {
+  bf16* out[kMaxSp];
+  int ld, col0, pl, pl_loc, nl, img0;
+};
+
 struct Bars {
   uint64_t q_full, slot_full[SLOTS], slot_empty[SLOTS];
   uint64_t s_full[2][2], p_full[2][2];  // [tile][S buffer]
@@ -76,7 +82,7 @@ struct Bars {
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
-                int b0, int b1, int width, float scale_log2, int* status) {
+                int b0, int b1, int width, float scale_log2, const SpOut spo, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
@@ -327,7 +333,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (ok && mbar_wait_uniform(&bars->o_full[x], 0, abort_flag, status, STATUS_TIMEOUT_ATTN)) {
       tc_fence_after();
       const float inv = 1.f / lsum;
-      bf16* dst = out + (static_cast<long long>(sample) * nq + qi) * width + head * 128;
+      bf16* dst;
+      if (spo.out[0] != nullptr) {  // sequence-parallel: the row's owner, at this rank's head columns
+        int owner, local;
+        if (qi < spo.img0) {
+          owner = qi / spo.pl;
+          local = qi - owner * spo.pl;
+        } else {
+          const int i = qi - spo.img0;
+          owner = i / spo.nl;
+          local = spo.pl_loc + (i - owner * spo.nl);
+        }
+        dst = spo.out[owner < kMaxSp ? owner : 0] + static_cast<long long>(local) * spo.ld + spo.col0 + head * 128;
+      } else {
+        dst = out + (static_cast<long long>(sample) * nq + qi) * width + head * 128;
+      }
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t rr[32];
@@ -342,6 +362,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                               pack_bf16x2(__uint_as_float(rr[8 * i + 6]) * inv, __uint_as_float(rr[8 * i + 7]) * inv));
         }
       }
+      if (spo.out[0] != nullptr) __threadfence_system();  // peer stores performed before the pass's barrier
     }
   }
   tc_fence_before();
@@ -373,8 +394,17 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
   dim3 grid((a.nq + 2 * TILE - 1) / (2 * TILE), a.heads, a.batch);
+  SpOut spo;
+  for (int i = 0; i < kMaxSp; ++i) spo.out[i] = a.sp_out[i];
+  spo.ld = a.sp_ld;
+  spo.col0 = a.sp_col0;
+  spo.pl = a.sp_pl;
+  spo.pl_loc = a.sp_pl_loc;
+  spo.nl = a.sp_nl;
+  spo.img0 = a.sp_img0;
+  if (spo.out[0] != nullptr && (a.batch != 1 || spo.nl <= 0 || (spo.img0 > 0 && spo.pl <= 0))) return -1;
   k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
-                                                   a.scale_log2, d_status);
+                                                   a.scale_log2, spo, d_status);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -109,6 +109,7 @@ struct NcclApi {
   ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -137,6 +138,7 @@ NcclApi& nccl() {
     api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
     api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
     api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+    api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
     api.ok = ok;
     if (!ok) api.why = "libnccl.so.2 lacks a symbol this library uses";
@@ -146,18 +148,23 @@ NcclApi& nccl() {
 
 // buffers of a sequence-parallel (Ulysses) pass on one rank
 struct SpBufs {
-  void* mem = nullptr;
+  void* mem = nullptr;       // one allocation, the same layout on every rank (peers address it by offset)
   int cap_nloc = 0, cap_ntot = 0, cap_p = 0, cap_n = 0, cap_wg = 0;
   float* xp = nullptr;       // every prefix row's x on step 1 [P][W]
-  bf16 *sq = nullptr, *sk = nullptr, *sv = nullptr;  // grouped send buffers [G][n_loc][Wg]
-  bf16* qf = nullptr;        // this rank's heads, every row of the pass [n_tot][Wg]
-  bf16* af = nullptr;        // attention out, same layout
-  bf16* ab = nullptr;        // attention out of this rank's rows, back by head group [G][n_loc][Wg]
+  bf16* qf = nullptr;        // this rank's heads, every row of the pass [n_tot][Wg]: every rank's QKV stores here
+  bf16* att_in = nullptr;    // attention out of this rank's rows, all heads [n_loc][W]: every rank's attention
+                             // stores its heads' columns here
   float2* rope = nullptr;    // RoPE of this rank's rows [n_loc][64]
   float* zslice = nullptr;   // [64][N/G]
   float* zall = nullptr;     // [G][64][N/G]
+  int* bar = nullptr;        // one int the pass's barriers all-reduce
+  size_t off_qf = 0, off_att = 0;
   bf16* kv = nullptr;        // [layer][K or V][L][Wg]: this rank's heads of the whole sequence
   int kv_l = 0;
+  // every rank's mem and kv mapped into this process (CUDA IPC; this rank's own at its index)
+  char* peer_mem[kMaxSp] = {};
+  bf16* peer_kv[kMaxSp] = {};
+  bool mapped = false;
 };
 
 }  // namespace
@@ -745,11 +752,90 @@ int nccl_settle(exn_handle* h, ncclComm_t comm, const char* what) {
   }
 }
 
+// A barrier of the sequence-parallel group on the handle's stream: a one-int all-reduce.  What a
+// rank's kernels stored into peers' memory before it (each writer fences at system scope) is
+// visible to every rank's kernels after it.
+int check_status(exn_handle* h);
+
+int sp_barrier(exn_handle* h, const char* what) {
+  const ncclResult_t nr = nccl().AllReduce(h->sp.bar, h->sp.bar, 1, ncclInt32, ncclSum, h->comm, h->st);
+  if (nr != ncclSuccess && nr != ncclInProgress) return nccl_fail(h, nr, what);
+  return nccl_settle(h, h->comm, what);
+}
+
+// Unmap the peers' buffers (after this rank's queued work is done).
+void sp_unmap(exn_handle* h) {
+  SpBufs& b = h->sp;
+  if (b.mapped) {
+    cudaStreamSynchronize(h->st);
+    for (int g = 0; g < h->world && g < kMaxSp; ++g) {
+      if (g == h->rank) continue;
+      if (b.peer_mem[g]) cudaIpcCloseMemHandle(b.peer_mem[g]);
+      if (b.peer_kv[g]) cudaIpcCloseMemHandle(b.peer_kv[g]);
+    }
+  }
+  for (int g = 0; g < kMaxSp; ++g) {
+    b.peer_mem[g] = nullptr;
+    b.peer_kv[g] = nullptr;
+  }
+  b.mapped = false;
+}
+
+// Export this rank's mem and kv (CUDA IPC handles), all-gather every rank's over the communicator
+// and map the peers', so kernels can store straight into any rank's buffers over NVLink.
+int sp_map(exn_handle* h) {
+  SpBufs& b = h->sp;
+  const int G = h->world, r = h->rank;
+  cudaIpcMemHandle_t mine[2];
+  CK(cudaIpcGetMemHandle(&mine[0], b.mem));
+  CK(cudaIpcGetMemHandle(&mine[1], b.kv));
+  const size_t hb = sizeof mine;
+  std::vector<char> all(hb * G);
+  char* d = nullptr;
+  CK(cudaMalloc(&d, hb * G));
+  CK(cudaMemcpyAsync(d + hb * r, mine, hb, cudaMemcpyHostToDevice, h->st));
+  const ncclResult_t nr = nccl().AllGather(d + hb * r, d, hb, ncclUint8, h->comm, h->st);
+  int rc = EXN_OK;
+  if (nr != ncclSuccess && nr != ncclInProgress) rc = nccl_fail(h, nr, "exchange of the peer buffers");
+  if (!rc) rc = nccl_settle(h, h->comm, "exchange of the peer buffers");
+  if (!rc) rc = check_status(h);
+  if (!rc && cudaMemcpy(all.data(), d, hb * G, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = fail(h, EXN_ECUDA, "exchange of the peer buffers: copy failed");
+  cudaFree(d);
+  if (rc) return rc;
+  for (int g = 0; g < G; ++g) {
+    if (g == r) {
+      b.peer_mem[g] = static_cast<char*>(b.mem);
+      b.peer_kv[g] = b.kv;
+      continue;
+    }
+    cudaIpcMemHandle_t th[2];
+    std::memcpy(th, all.data() + hb * g, hb);
+    void* pm = nullptr;
+    void* pk = nullptr;
+    CK(cudaIpcOpenMemHandle(&pm, th[0], cudaIpcMemLazyEnablePeerAccess));
+    b.peer_mem[g] = static_cast<char*>(pm);
+    CK(cudaIpcOpenMemHandle(&pk, th[1], cudaIpcMemLazyEnablePeerAccess));
+    b.peer_kv[g] = static_cast<bf16*>(pk);
+  }
+  b.mapped = true;
+  return EXN_OK;
+}
+
 int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
   const exn_config& c = h->cfg;
   const int G = h->world, W = c.width, Wg = W / G;
   SpBufs& b = h->sp;
-  if (n_loc > b.cap_nloc || n_tot > b.cap_ntot || P > b.cap_p || N > b.cap_n || Wg != b.cap_wg) {
+  const bool grow_mem = n_loc > b.cap_nloc || n_tot > b.cap_ntot || P > b.cap_p || N > b.cap_n || Wg != b.cap_wg;
+  const bool grow_kv = L > b.kv_l;
+  int rc;
+  // every rank takes the same decisions here (same arguments on every rank); before anyone frees
+  // a buffer, every peer has unmapped it
+  if ((grow_mem || grow_kv) && b.mapped) {
+    sp_unmap(h);
+    if ((rc = sp_barrier(h, "unmapping the peer buffers")) || (rc = check_status(h))) return rc;
+  }
+  if (grow_mem) {
     const int NL = std::max(n_loc, b.cap_nloc), NT = std::max(n_tot, b.cap_ntot), PP = std::max(P, b.cap_p),
               NN = std::max(N, b.cap_n);
     size_t off = 0;
@@ -758,24 +844,22 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
       off += al(bytes);
       return o;
     };
-    const size_t oxp = take(size_t(std::max(PP, 1)) * W * 4), osq = take(size_t(NL) * W * 2),
-                 osk = take(size_t(NL) * W * 2), osv = take(size_t(NL) * W * 2), oqf = take(size_t(NT) * Wg * 2),
-                 oaf = take(size_t(NT) * Wg * 2), oab = take(size_t(NL) * W * 2), orp = take(size_t(NL) * 64 * 8),
-                 ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4);
+    const size_t oxp = take(size_t(std::max(PP, 1)) * W * 4), oqf = take(size_t(NT) * Wg * 2),
+                 oat = take(size_t(NL) * W * 2), orp = take(size_t(NL) * 64 * 8),
+                 ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4), obar = take(sizeof(int));
     if (b.mem) cudaFree(b.mem);
     b.mem = nullptr;
     CK(cudaMalloc(&b.mem, off));
     char* m = static_cast<char*>(b.mem);
     b.xp = reinterpret_cast<float*>(m + oxp);
-    b.sq = reinterpret_cast<bf16*>(m + osq);
-    b.sk = reinterpret_cast<bf16*>(m + osk);
-    b.sv = reinterpret_cast<bf16*>(m + osv);
     b.qf = reinterpret_cast<bf16*>(m + oqf);
-    b.af = reinterpret_cast<bf16*>(m + oaf);
-    b.ab = reinterpret_cast<bf16*>(m + oab);
+    b.att_in = reinterpret_cast<bf16*>(m + oat);
     b.rope = reinterpret_cast<float2*>(m + orp);
     b.zslice = reinterpret_cast<float*>(m + ozs);
     b.zall = reinterpret_cast<float*>(m + oza);
+    b.bar = reinterpret_cast<int*>(m + obar);
+    b.off_qf = oqf;
+    b.off_att = oat;
     b.cap_nloc = NL;
     b.cap_ntot = NT;
     b.cap_p = PP;
@@ -798,10 +882,12 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
     b.kv = nk;
     b.kv_l = L;
   }
+  if (!b.mapped && (rc = sp_map(h))) return rc;
   return EXN_OK;
 }
 
 void free_sp(exn_handle* h) {
+  sp_unmap(h);
   if (h->sp.mem) cudaFree(h->sp.mem);
   if (h->sp.kv) cudaFree(h->sp.kv);
   h->sp = SpBufs();
@@ -832,7 +918,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
   if ((rc = ensure_sp(h, n_loc, n_tot, P, N, L))) return rc;
   SpBufs& b = h->sp;
   const size_t kv_layer = size_t(2) * b.kv_l * Wg;
-  h->launches += 5 + 3 + 8LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
+  h->launches += 5 + 3 + 7LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
 
   // timestep
   temb_launch(h->emb, in.sigma, c.freq, h->st);
@@ -882,47 +968,37 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     rope_table_launch(b.rope, P + r * Nl, n_loc, P, in.hh, in.ww, in.nref ? in.a : 0, in.nref ? in.rh : 0,
                       in.nref ? in.rw : 0, h->st);
 
-  NcclApi& nc = nccl();
-  const size_t chunk = size_t(n_loc) * Wg;  // elements of one rank-to-rank piece of a grouped buffer
-  auto bytes = [](size_t elems) { return elems * 2; };
   for (int il = 0; il < c.layers; ++il) {
-    bf16* kl = b.kv + il * kv_layer;
-    bf16* vl = kl + size_t(b.kv_l) * Wg;
+    const size_t kl_off = il * kv_layer;
     ln_mod_launch(h->x, h->y, h->modv + 0 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
+    // QKV: every row's head group g stored by the epilogue straight into rank g's Q and K/V (over
+    // NVLink for g != r), at the row's place in the sequence; the all-to-all is the GEMM's stores
     GemmEpi eq;
     eq.seg_in = n_loc;
     eq.width = W;
     eq.norm_q = h->norm_q + il * c.head_dim;
     eq.norm_k = h->norm_k + il * c.head_dim;
     eq.rope = b.rope;
-    eq.q = b.sq;
-    eq.k = b.sk;
-    eq.v = b.sv;
     eq.group_w = Wg;
+    for (int g = 0; g < G; ++g) {
+      eq.sp_q[g] = reinterpret_cast<bf16*>(b.peer_mem[g] + b.off_qf);
+      eq.sp_k[g] = b.peer_kv[g] + kl_off;
+      eq.sp_v[g] = b.peer_kv[g] + kl_off + size_t(b.kv_l) * Wg;
+    }
+    eq.sp_rank = r;
+    eq.sp_pl = pl;
+    eq.sp_pl_loc = pl_loc;
+    eq.sp_nl = Nl;
+    eq.sp_img0 = img0;
+    eq.sp_p = P;
     if ((rc = gemm(h, h->y, W, h->w_qkv + static_cast<size_t>(il) * 3 * W * W, W, n_loc, 3 * W, W, EPI_QKV, eq)))
       return rc;
-    // all-to-all: my rows' head group s to rank s; rank s's rows of my head group into every row's place
-    nc.GroupStart();
-    for (int sr = 0; sr < G; ++sr) {
-      const bf16* src[3] = {b.sq + sr * chunk, b.sk + sr * chunk, b.sv + sr * chunk};
-      bf16* dst_pre[3] = {b.qf + size_t(sr) * pl * Wg, kl + size_t(sr) * pl * Wg, vl + size_t(sr) * pl * Wg};
-      bf16* dst_img[3] = {b.qf + size_t(img0 + sr * Nl) * Wg, kl + size_t(P + sr * Nl) * Wg, vl + size_t(P + sr * Nl) * Wg};
-      for (int t = 0; t < 3; ++t) {
-        if (pl_loc) {
-          nc.Send(src[t], bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
-          nc.Recv(dst_pre[t], bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
-        }
-        nc.Send(src[t] + size_t(pl_loc) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
-        nc.Recv(dst_img[t], bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
-      }
-    }
-    nc.GroupEnd();
-    if ((rc = nccl_settle(h, h->comm, "all-to-all before attention"))) return rc;
+    if ((rc = sp_barrier(h, "barrier before attention"))) return rc;
     AttnArgs aa;
     aa.q = b.qf;
-    aa.k = kl;
-    aa.v = vl;
-    aa.out = b.af;
+    aa.k = b.kv + kl_off;
+    aa.v = b.kv + kl_off + size_t(b.kv_l) * Wg;
+    aa.out = b.att_in;
     aa.nq = n_tot;
     aa.q0 = q0;
     aa.p = P;
@@ -933,21 +1009,16 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     aa.width = Wg;
     aa.kv_rows = b.kv_l;
     aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    // each output row stored into the rank that keeps it, at this rank's head columns
+    for (int g = 0; g < G; ++g) aa.sp_out[g] = reinterpret_cast<bf16*>(b.peer_mem[g] + b.off_att);
+    aa.sp_ld = W;
+    aa.sp_col0 = r * Wg;
+    aa.sp_pl = pl;
+    aa.sp_pl_loc = pl_loc;
+    aa.sp_nl = Nl;
+    aa.sp_img0 = img0;
     if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
-    // all-to-all back: rank s's rows of my heads to s; my rows of rank s's heads into group s
-    nc.GroupStart();
-    for (int sr = 0; sr < G; ++sr) {
-      bf16* back = b.ab + sr * chunk;
-      if (pl_loc) {
-        nc.Send(b.af + size_t(sr) * pl * Wg, bytes(size_t(pl) * Wg), ncclUint8, sr, h->comm, h->st);
-        nc.Recv(back, bytes(size_t(pl_loc) * Wg), ncclUint8, sr, h->comm, h->st);
-      }
-      nc.Send(b.af + size_t(img0 + sr * Nl) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
-      nc.Recv(back + size_t(pl_loc) * Wg, bytes(size_t(Nl) * Wg), ncclUint8, sr, h->comm, h->st);
-    }
-    nc.GroupEnd();
-    if ((rc = nccl_settle(h, h->comm, "all-to-all after attention"))) return rc;
-    group_gather_launch(b.ab, h->att, G, n_loc, Wg, h->st);
+    if ((rc = sp_barrier(h, "barrier after attention"))) return rc;
     GemmEpi eo;
     eo.out = h->x;
     eo.ld_out = W;
@@ -956,7 +1027,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     eo.mod_stride = 4 * W;
     eo.n0 = 0;
     eo.p = pl_loc;
-    if ((rc = gemm(h, h->att, W, h->w_out + static_cast<size_t>(il) * W * W, W, n_loc, W, W, EPI_GATE_RESID, eo)))
+    if ((rc = gemm(h, b.att_in, W, h->w_out + static_cast<size_t>(il) * W * W, W, n_loc, W, W, EPI_GATE_RESID, eo)))
       return rc;
     ln_mod_launch(h->x, h->y, h->modv + 2 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
     GemmEpi eg;

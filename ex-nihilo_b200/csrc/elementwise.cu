@@ -424,24 +424,6 @@ void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, in
                                                                                     ref_h, ref_w, split, r1);
 }
 
-// in [G][n][gw] -> out [n][G*gw], 16 bytes a thread
-__global__ void k_group_gather(const uint4* __restrict__ in, uint4* __restrict__ out, int groups, int n, int gw8) {
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(groups) * n * gw8;
-  if (idx >= total) return;
-  const int c = static_cast<int>(idx % gw8);
-  const long long rest = idx / gw8;
-  const int t = static_cast<int>(rest % n), g = static_cast<int>(rest / n);
-  out[(static_cast<long long>(t) * groups + g) * gw8 + c] = in[idx];
-}
-
-void group_gather_launch(const bf16* in, bf16* out, int groups, int n, int gw, cudaStream_t st) {
-  const long long total = static_cast<long long>(groups) * n * (gw / 8);
-  if (total <= 0) return;
-  k_group_gather<<<blocks_for(total, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out),
-                                                         groups, n, gw / 8);
-}
-
 void temb_launch(float* emb, double sigma, int freq, cudaStream_t st) {
   k_temb<<<1, 128, 0, st>>>(emb, 1000.0 * sigma, freq);
 }

@@ -23,6 +23,9 @@ enum EpiKind : int {
   EPI_PROJ = 6,        // v channel-major and/or z += dsigma * v              (proj_out)
 };
 
+// ranks of a sequence-parallel group that kernels address directly (peer pointers)
+constexpr int kMaxSp = 16;
+
 // GEMM row r maps to output row
 //   (r / seg_in) * seg_out + off + t + (t >= split_at ? split_gap : 0),  t = r % seg_in
 struct GemmEpi {
@@ -42,9 +45,17 @@ struct GemmEpi {
   bf16* k = nullptr;
   bf16* v = nullptr;
   long long kv_sample_stride = 0;  // elements from one sample's K (V) rows to the next
-  // EPI_QKV, sequence-parallel: when group_w > 0, q, k and v are all written head-group-major,
-  // [world][seg_in rows][group_w], the layout an all-to-all sends whole (group g to rank g)
+  // EPI_QKV, sequence-parallel (group_w > 0): the tile's columns belong to head group
+  // g = column / group_w, kept by rank g; each row is stored straight into rank g's buffers
+  // (peer memory over NVLink): q at sp_q[g] + qrow * group_w, k and v at sp_k[g] / sp_v[g] +
+  // kvrow * group_w.  This rank's local row t is prefix row sp_rank * sp_pl + t when t <
+  // sp_pl_loc, else image row i = t - sp_pl_loc at qrow sp_img0 + sp_rank * sp_nl + i and
+  // kvrow sp_p + sp_rank * sp_nl + i (qrow = kvrow for prefix rows).
   int group_w = 0;
+  bf16* sp_q[kMaxSp] = {};
+  bf16* sp_k[kMaxSp] = {};
+  bf16* sp_v[kMaxSp] = {};
+  int sp_rank = 0, sp_pl = 0, sp_pl_loc = 0, sp_nl = 0, sp_img0 = 0, sp_p = 0;
   // EPI_PROJ
   float* z = nullptr;
   float* vout = nullptr;
@@ -75,6 +86,12 @@ struct AttnArgs {
   int heads = 0, width = 0;
   int kv_rows = 0;           // row capacity of one sample's K/V
   float scale_log2 = 0.f;    // log2(e) / sqrt(128)
+  // sequence-parallel (sp_out[0] != null): query row qi of the pass is stored into the rank that
+  // keeps it, at sp_out[owner] + local * sp_ld + sp_col0 + head * 128: prefix rows qi < sp_img0
+  // (first pass) belong to rank qi / sp_pl at local qi % sp_pl; image row i = qi - sp_img0 to
+  // rank i / sp_nl at local sp_pl_loc + i % sp_nl
+  bf16* sp_out[kMaxSp] = {};
+  int sp_ld = 0, sp_col0 = 0, sp_pl = 0, sp_pl_loc = 0, sp_nl = 0, sp_img0 = 0;
 };
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st);
 
@@ -93,8 +110,6 @@ void latent_rows_launch(const float* lat, bf16* rows, int batch, int channels, i
 // r0 + t (prefix), t >= split is sequence row r1 + (t - split) (image).
 void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, int ref_a, int ref_h, int ref_w,
                        cudaStream_t st, int split = 0, int r1 = 0);
-// in [G][n][gw] -> out [n][G*gw] (head groups back into columns), bf16
-void group_gather_launch(const bf16* in, bf16* out, int groups, int n, int gw, cudaStream_t st);
 // emb[2][freq]: timestep embedding of 1000*sigma and of 0
 void temb_launch(float* emb, double sigma, int freq, cudaStream_t st);
 // Weight kinds for the small GEMVs

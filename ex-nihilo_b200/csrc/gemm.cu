@@ -142,10 +142,18 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
     const int hc0 = col0 - sec * e.width;      // first column within q / k / v
     const int t = row % e.seg_in, b = row / e.seg_in;
     bf16* dst;
-    if (e.group_w > 0)
-      dst = (sec == 0 ? e.q : sec == 1 ? e.k : e.v) +
-            (static_cast<long long>(hc0 / e.group_w) * e.seg_in + row) * e.group_w + hc0 % e.group_w;
-    else if (sec == 0)
+    if (e.group_w > 0) {  // sequence-parallel: straight into the rank that keeps this head group
+      const int g = hc0 / e.group_w, cg = hc0 % e.group_w;
+      long long qrow, kvrow;
+      if (row < e.sp_pl_loc) {
+        qrow = kvrow = static_cast<long long>(e.sp_rank) * e.sp_pl + row;
+      } else {
+        const long long i = static_cast<long long>(e.sp_rank) * e.sp_nl + (row - e.sp_pl_loc);
+        qrow = e.sp_img0 + i;
+        kvrow = e.sp_p + i;
+      }
+      dst = sec == 0 ? e.sp_q[g] + qrow * e.group_w + cg : (sec == 1 ? e.sp_k[g] : e.sp_v[g]) + kvrow * e.group_w + cg;
+    } else if (sec == 0)
       dst = e.q + static_cast<long long>(row) * e.width + hc0;
     else
       dst = (sec == 1 ? e.k : e.v) + b * e.kv_sample_stride + static_cast<long long>(e.n0 + t) * e.width + hc0;
@@ -179,6 +187,7 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
 #pragma unroll
       for (int c = 0; c < 4; ++c) store_bf16x32(dst + hh * 128 + c * 32, v + c * 32);
     }
+    if (e.group_w > 0) __threadfence_system();  // peer stores performed before the pass's barrier
   } else if constexpr (EPI == EPI_PROJ) {
     static_assert(BN == 64, "proj_out has the latent's 64 channels");
     const int b = row / e.nimg, i = row - (row / e.nimg) * e.nimg;
