@@ -449,7 +449,7 @@ def run_edit(args):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Q8_0 weights (seed 1, bf16 in HBM); text, reference and noise ~N(0,1)",
         "config": {"workload": "BASELINE config 4: edit, 4096 target + 4096 reference + 512 text rows (8704), A=8, "
-                               "8 Euler steps, one picture over all GPUs (Ulysses, NCCL all-to-all)",
+                               "8 Euler steps, one picture over all GPUs (Ulysses; QKV and attention store rows into peer GPUs over NVLink)",
                    "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks, FFN 12288", "global_batch": 1, "seq_len": 8704,
                    "parallelism": "sp%d (Ulysses)" % world, "timing": "wall clock around exn_generate (host buffers)",
                    "algorithmic_tflop_per_picture": round((gf + af) / 1e12, 1)},
