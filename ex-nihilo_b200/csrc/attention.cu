@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
+  griddep_launch();
   // TMEM columns: S_a buffers [0,64) [64,128), S_b [128,192) [192,256), O_a [256,384), O_b [384,512)
 
   if (warp == 0) {
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tma_prefetch(&tmQ);
       tma_prefetch(&tmK);
       tma_prefetch(&tmV);
+      griddep_wait();  // Q, K and V are the previous kernel's output
       const int hx = head * 128;
       mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
       for (int x = 0; x < 2; ++x)
@@ -403,9 +405,8 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   spo.nl = a.sp_nl;
   spo.img0 = a.sp_img0;
   if (spo.out[0] != nullptr && (a.batch != 1 || spo.nl <= 0 || (spo.img0 > 0 && spo.pl <= 0))) return -1;
-  k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(tq, tk, tv, a.out, a.nq, a.q0, a.p, a.l, a.b0, a.b1, a.width,
-                                                   a.scale_log2, spo, d_status);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(k_attention, grid, dim3(ATT_THREADS), ATT_SMEM, st, tq, tk, tv, a.out, a.nq, a.q0,
+                                     a.p, a.l, a.b0, a.b1, a.width, a.scale_log2, spo, d_status));
 }
 
 }  // namespace exn

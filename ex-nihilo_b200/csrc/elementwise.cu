@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(LN_THREADS) k_ln_mod(const float* __restrict__
                                                       int width, int seg_in, int seg_out, int off, int n0, int p,
                                                       int single) {
   __shared__ float red[LN_THREADS / 32];
+  griddep_launch();
+  griddep_wait();  // x is the previous kernel's output, y its input
   const int r = blockIdx.x;
   if (r >= rows) return;
   const int b = r / seg_in, t = r - b * seg_in;
@@ -403,7 +405,8 @@ inline unsigned blocks_for(long long n, int t) { return static_cast<unsigned>((n
 void ln_mod_launch(const float* x, bf16* y, const float* scale, int mod_stride, int rows, int width, int seg_in,
                    int seg_out, int off, int n0, int p, int single, cudaStream_t st) {
   if (rows <= 0) return;
-  k_ln_mod<<<rows, LN_THREADS, 0, st>>>(x, y, scale, mod_stride, rows, width, seg_in, seg_out, off, n0, p, single);
+  launch_pdl(k_ln_mod, dim3(rows), dim3(LN_THREADS), 0, st, x, y, scale, mod_stride, rows, width, seg_in, seg_out, off,
+             n0, p, single);
 }
 
 void rms_launch(const float* x, const float* w, bf16* y, int rows, int width, cudaStream_t st) {

@@ -145,6 +145,16 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ----------------------------------------------------------------------------- dependent launch
+// Kernels launched with launch_pdl (exn_internal.h) may start while the kernel before them on the
+// stream is still finishing.  Each one lets its own successor launch as soon as all of its CTAs
+// have started (griddep_launch at entry: a successor CTA can then take only an SM that this kernel
+// no longer needs), and reads or writes nothing that the previous kernel writes or reads until
+// griddep_wait returns, which is when the previous kernel has completed and its writes are
+// visible.  Set-up (barriers, TMEM, tensor-map prefetch) runs before the wait.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ----------------------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {

@@ -26,6 +26,25 @@ enum EpiKind : int {
 // ranks of a sequence-parallel group that kernels address directly (peer pointers)
 constexpr int kMaxSp = 16;
 
+// Launch KERNEL with programmatic dependent launch allowed: it may begin while the previous kernel
+// on ST finishes; the kernel itself must call griddep_wait (exn_device.cuh) before touching
+// anything the previous kernel reads or writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // GEMM row r maps to output row
 //   (r / seg_in) * seg_out + off + t + (t >= split_at ? split_gap : 0),  t = r % seg_in
 struct GemmEpi {

@@ -258,10 +258,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer
+      // ---- TMA producer: the previous kernel's outputs (A, and the epilogue's rows) are ready
+      griddep_wait();
       int stage = 0;
       uint32_t phase = 0;
       int last_phase[C::STAGES];
@@ -431,10 +433,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer (both CTAs)
+      // ---- TMA producer (both CTAs): the previous kernel's outputs (A, and the epilogue's rows) are ready
+      griddep_wait();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -593,8 +597,8 @@ static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t
   int group_m = static_cast<int>((48ll << 20) / (static_cast<long long>(BM) * g.K * 2));
   group_m = group_m < 8 ? 8 : group_m;
   group_m = group_m > num_m ? num_m : group_m;
-  k_gemm<BN, EPI><<<grid, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, group_m, g.ep, d_status);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(k_gemm<BN, EPI>, dim3(grid), dim3(GEMM_THREADS), C::SMEM, st, ta, tb, g.M, g.N,
+                                     g.K, group_m, g.ep, d_status));
 }
 
 template <int EPI>
@@ -621,8 +625,8 @@ static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream
   int group_m = static_cast<int>((48ll << 20) / (256ll * g.K * 2));
   group_m = group_m < 4 ? 4 : group_m;
   group_m = group_m > num_m ? num_m : group_m;
-  k_gemm2<EPI><<<clusters * 2, GEMM_THREADS, C::SMEM, st>>>(ta, tb, g.M, g.N, g.K, group_m, g.ep, d_status);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_pdl(k_gemm2<EPI>, dim3(clusters * 2), dim3(GEMM_THREADS), C::SMEM, st, ta, tb,
+                                     g.M, g.N, g.K, group_m, g.ep, d_status));
 }
 
 static bool use_pairs() {
