@@ -1,9 +1,9 @@
-"""Sequence parallelism (Ulysses) over 2 GPUs: the rows of one picture split
-between two processes, Q/K/V and the attention output exchanged by NCCL
-all-to-all.  Every row's arithmetic is the one-GPU arithmetic, so the result
-must equal a one-GPU handle's bit for bit (rel-L2 < 1e-6): plain and edit
-layouts, the first pass and a cached one, the fused 8-step loop.  Needs two
-GPUs; NVLS off (a rank's failure must not leave NVLink multicast state)."""
+"""Sequence parallelism (Ulysses) over 2 (and, where there are 4, 4) GPUs: the rows of one
+picture split between the processes, Q/K/V and the attention output stored by the QKV GEMM and
+the attention kernel straight into the rank that keeps them (peer memory over NVLink).  Every
+row's arithmetic is the one-GPU arithmetic, so the result must equal a one-GPU handle's bit for
+bit (rel-L2 < 1e-6): plain and edit layouts, the first pass and a cached one, the fused 8-step
+loop.  NVLS off (a rank's failure must not leave NVLink multicast state)."""
 import os
 import traceback
 
@@ -14,12 +14,21 @@ pytestmark = pytest.mark.gpu
 SHAPE = dict(width=512, layers=2, ffn=1536, context=512)
 
 
-def _two_gpus():
+def _gpus():
     try:
         import torch
-        return torch.cuda.device_count() >= 2
+        return torch.cuda.device_count()
     except Exception:
-        return False
+        return 0
+
+
+def _two_gpus():
+    return _gpus() >= 2
+
+
+# world size -> (DiT shape, reference picture h, w): width / world a multiple of 256, and the
+# prefix (8 text rows + the reference's) and image (4 x 6) rows divisible by the world size
+CASES = {2: (SHAPE, 2, 3), 4: (dict(width=1024, layers=2, ffn=3072, context=512), 2, 2)}
 
 
 def _rank(rank, world, uid, q):
@@ -27,9 +36,10 @@ def _rank(rank, world, uid, q):
     try:
         import exn_b200 as E
         from oracle import dit_oracle as O
-        sh = O.Shape(**SHAPE)
+        shape, rh, rw = CASES[world]
+        sh = O.Shape(**shape)
         out = {}
-        with E.Dit(device=rank, **SHAPE) as d:
+        with E.Dit(device=rank, **shape) as d:
             d.load_synthetic(1)
             d.comm_init(uid, rank, world)
             p, h, w = 8, 4, 6
@@ -37,22 +47,24 @@ def _rank(rank, world, uid, q):
             out["v1"] = d.velocity(ctx[0], p, lat[0], h, w, 0.9, prefix_key="k")
             out["v2"] = d.velocity(ctx[0], p, lat[0] * 0.5, h, w, 0.7, prefix_key="k")     # cached prefix
             out["z"] = d.generate(ctx[0], p, lat[0], h, w, prefix_key="g")
-            _, rl = O.synth_inputs(sh, 1, 2, 3, seed=4)
-            out["ve"] = d.velocity(ctx[0], p, lat[0], h, w, 0.8, prefix_key=("e", 1), ref=(2, rl[0], 2, 3))
+            _, rl = O.synth_inputs(sh, 1, rh, rw, seed=4)
+            out["ve"] = d.velocity(ctx[0], p, lat[0], h, w, 0.8, prefix_key=("e", 1), ref=(2, rl[0], rh, rw))
         q.put((rank, out, None))
     except Exception:
         q.put((rank, None, traceback.format_exc()))
 
 
-@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
-def test_two_rank_sequence_parallel_equals_one_gpu():
+@pytest.mark.parametrize("world", [2, 4])
+def test_sequence_parallel_equals_one_gpu(world):
+    if _gpus() < world:
+        pytest.skip("needs %d GPUs" % world)
     import torch.multiprocessing as mp
     import exn_b200 as E
     from oracle import dit_oracle as O
     uid = E.comm_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, q)) for r in range(world)]
     for pr in procs:
         pr.start()
     res = {}
@@ -63,18 +75,19 @@ def test_two_rank_sequence_parallel_equals_one_gpu():
     for pr in procs:
         pr.join(timeout=60)
         assert pr.exitcode == 0
-    sh = O.Shape(**SHAPE)
+    shape, rh, rw = CASES[world]
+    sh = O.Shape(**shape)
     p, h, w = 8, 4, 6
     c, lat = O.synth_inputs(sh, p, h, w, seed=3)
-    _, rl = O.synth_inputs(sh, 1, 2, 3, seed=4)
-    with E.Dit(device=0, **SHAPE) as d:
+    _, rl = O.synth_inputs(sh, 1, rh, rw, seed=4)
+    with E.Dit(device=0, **shape) as d:
         d.load_synthetic(1)
         want = {"v1": d.velocity(c[0], p, lat[0], h, w, 0.9, prefix_key="k"),
                 "v2": d.velocity(c[0], p, lat[0] * 0.5, h, w, 0.7, prefix_key="k"),
                 "z": d.generate(c[0], p, lat[0], h, w, prefix_key="g"),
-                "ve": d.velocity(c[0], p, lat[0], h, w, 0.8, prefix_key=("e", 1), ref=(2, rl[0], 2, 3))}
+                "ve": d.velocity(c[0], p, lat[0], h, w, 0.8, prefix_key=("e", 1), ref=(2, rl[0], rh, rw))}
     for key, v in want.items():
-        for r in (0, 1):
+        for r in range(world):
             assert O.rel_l2(res[r][key], v) < 1e-6, (key, r, O.rel_l2(res[r][key], v))
 
 
