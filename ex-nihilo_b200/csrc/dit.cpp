@@ -213,6 +213,9 @@ struct exn_handle {
   size_t trace_floats = 0;
   Profile prof;
   double last_ms[4] = {0, 0, 0, 0};  // GEMM (other than gate_up), attention, other, gate_up GEMM
+  // device time of the last exn_velocity / exn_generate: inputs uploaded .. result ready to copy back
+  cudaEvent_t call_ev[2] = {nullptr, nullptr};
+  double last_call_ms = 0;
   long long launches = 0;  // kernels of this library queued by the step code since open
 
   // sequence parallelism over `world` handles (one per GPU)
@@ -1133,6 +1136,20 @@ int upload_inputs(exn_handle* h, const float* context, int p, const float* laten
   return EXN_OK;
 }
 
+// Events on the handle's stream around the device part of a host-buffer call (I = 0 after the
+// inputs' upload, 1 before the result's download).
+int mark_call(exn_handle* h, int i) {
+  if (!h->call_ev[i]) CK(cudaEventCreate(&h->call_ev[i]));
+  CK(cudaEventRecord(h->call_ev[i], h->st));
+  return EXN_OK;
+}
+
+// After the call's stream has drained: the device time between the two marks.
+void read_call_time(exn_handle* h) {
+  float ms = 0.f;
+  h->last_call_ms = cudaEventElapsedTime(&ms, h->call_ev[0], h->call_ev[1]) == cudaSuccess ? ms : 0.0;
+}
+
 }  // namespace
 
 // ============================================================================ C ABI
@@ -1208,6 +1225,8 @@ void exn_close(exn_handle* h) {
   if (h->slab) cudaFree(h->slab);
   if (h->d_status) cudaFree(h->d_status);
   for (auto& m : h->prof.marks) cudaEventDestroy(m.first);
+  for (cudaEvent_t e : h->call_ev)
+    if (e) cudaEventDestroy(e);
   if (h->st) cudaStreamDestroy(h->st);
   delete h;
 }
@@ -1415,7 +1434,7 @@ int exn_velocity(exn_handle* h, const float* context, int p, const float* latent
   const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
   const bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len &&
                       (h->comm ? true : h->kv_batch == 1);
-  if ((rc = upload_inputs(h, context, p, latent, hh, ww, ref, !cached))) return rc;
+  if ((rc = upload_inputs(h, context, p, latent, hh, ww, ref, !cached)) || (rc = mark_call(h, 0))) return rc;
   if (!cached) {
     h->prefix_valid = false;
     h->prefix_key = 0;
@@ -1436,8 +1455,10 @@ int exn_velocity(exn_handle* h, const float* context, int p, const float* latent
   in.v = h->vout;
   if ((rc = run_pass(h, in))) return rc;
   if (h->comm && h->world > 1 && (rc = sp_gather_columns(h, h->vout, hh * ww))) return rc;
+  if ((rc = mark_call(h, 1))) return rc;
   CK(cudaMemcpyAsync(v_out, h->vout, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
   if ((rc = check_status(h))) return rc;
+  read_call_time(h);
   if (prefix_key && !cached) {
     h->prefix_key = prefix_key;
     h->prefix_len = pfx;
@@ -1455,7 +1476,7 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
   const int nref = ref ? ref->rh * ref->rw : 0, pfx = p + nref;
   bool cached = prefix_key && h->prefix_valid && prefix_key == h->prefix_key && pfx == h->prefix_len &&
                 (h->comm ? true : h->kv_batch == 1);
-  if ((rc = upload_inputs(h, context, p, z, hh, ww, ref, true))) return rc;
+  if ((rc = upload_inputs(h, context, p, z, hh, ww, ref, true)) || (rc = mark_call(h, 0))) return rc;
   for (int s = 0; s + 1 < nsig; ++s) {
     if (!cached) {
       h->prefix_valid = false;
@@ -1485,12 +1506,14 @@ int exn_generate(exn_handle* h, const float* context, int p, float* z, int hh, i
     }
   }
   if (h->comm && h->world > 1 && (rc = sp_gather_columns(h, h->lat_dev, hh * ww))) return rc;
+  if ((rc = mark_call(h, 1))) return rc;
   CK(cudaMemcpyAsync(z, h->lat_dev, size_t(hh) * ww * h->cfg.latent * 4, cudaMemcpyDeviceToHost, h->st));
   if ((rc = check_status(h))) {
     h->prefix_valid = false;
     h->prefix_key = 0;
     return rc;
   }
+  read_call_time(h);
   return EXN_OK;
 }
 
@@ -1765,6 +1788,12 @@ int exn_test_profile(exn_handle* h, int on) {
 }
 
 long long exn_test_launch_count(const exn_handle* h) { return h ? h->launches : -1; }
+
+int exn_test_last_call_ms(const exn_handle* h, double* ms) {
+  if (!h || !ms) return EXN_EINVAL;
+  *ms = h->last_call_ms;
+  return EXN_OK;
+}
 
 int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms, double* gateup_ms) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_last_profile: null handle");

@@ -105,6 +105,7 @@ def lib():
         "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 4),
         "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_launch_count": (ctypes.c_longlong, [H]),
+        "exn_test_last_call_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(L, name)
@@ -278,6 +279,12 @@ class Dit:
 
     def launch_count(self):
         return int(lib().exn_test_launch_count(self.h))
+
+    def last_call_ms(self):
+        """Device time of the last velocity / generate call, inputs in HBM (ms)."""
+        ms = ctypes.c_double()
+        self._ck(lib().exn_test_last_call_ms(self.h, ctypes.byref(ms)))
+        return ms.value
 
 
 # ---- the reference's names

@@ -54,6 +54,12 @@ int exn_test_profile(exn_handle* h, int on);
 /* Kernels of this library the handle has queued since it was opened. */
 long long exn_test_launch_count(const exn_handle* h);
 
+/* Device time in ms (CUDA events on the handle's stream) of the last
+ * successful exn_velocity / exn_generate: from the end of the inputs' upload
+ * to the start of the result's download, so the DiT forwards (and, across
+ * GPUs, the gather of the latent) with the inputs already in HBM. */
+int exn_test_last_call_ms(const exn_handle* h, double* ms);
+
 /* Kernel time of the last exn_generate* / exn_velocity call in ms per
  * category when timing is on, else zeros: every GEMM, attention, the rest,
  * and of the GEMMs the gate_up + SwiGLU ones alone. */

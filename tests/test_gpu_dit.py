@@ -134,6 +134,19 @@ def test_edit_reference_matches_oracle(tiny, tiny_sw):
     assert O.rel_l2(v2, want2) < TOL
 
 
+def test_last_call_time_is_the_device_part(tiny):
+    # the device time of a host-buffer call: positive and within the call's own wall clock
+    import time
+    sh = O.Shape(**TINY)
+    p, h, w = 8, 4, 6
+    ctx, lat = O.synth_inputs(sh, p, h, w, seed=31)
+    t0 = time.perf_counter()
+    tiny.generate(ctx[0], p, lat[0], h, w)
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    ms = tiny.last_call_ms()
+    assert 0.0 < ms <= wall_ms
+
+
 def test_batch_equals_single(tiny):
     sh = O.Shape(**TINY)
     p, h, w, b = 8, 4, 6, 3

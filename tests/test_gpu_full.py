@@ -1,8 +1,9 @@
-"""The full-size DiT (D=4096, 32 blocks, 1024^2 = 64 x 64 latent, 128 text
-rows) on the B200: the 8-step latent against the
-reference's own ref_dit.py (tests/golden/cfg2_euler.npz, cosine >= 0.999)
-and size-independent properties (cached prefix == recomputed prefix; a
-batch == its pictures one by one)."""
+"""The full-size DiT (D=4096, 32 blocks) on the B200.  Config 2 (1024^2 = 64 x 64
+latent, 128 text rows): per-block parity with the fp32 oracle, the 8-step latent
+against the reference's own ref_dit.py (tests/golden/cfg2_euler.npz, cosine >=
+0.999) and size-independent properties (cached prefix == recomputed prefix; a
+batch == its pictures one by one).  Configs 3 (1536 x 1024, 256 text rows) and 4
+(an edit, 8704 rows): per-block parity with the oracle."""
 import json
 import os
 
@@ -36,29 +37,66 @@ def _golden():
     return np.load(GOLDEN)
 
 
+def _blocks_vs_oracle(d, p, h, w, ctx, lat, blocks, ref=None):
+    """Blocks BLOCKS of a sigma = 1 forward (the first pass: no cached prefix), each run by the
+    fp32 oracle from the GPU's own input to that block: [(block, rel-L2 of the output, rel-L2 of
+    the update)].  REF = (A, reference latent) for an edit (src/cuda-dit.lisp:137-192)."""
+    sh = O.Shape()
+    if ref is None:
+        pp, b0, b1, refpos, dref = p, 0, 0, None, None
+    else:
+        a, rl = ref
+        rh, rw = rl.shape[1:]
+        pp, b0, b1, refpos, dref = p + rh * rw, a, a + rh * rw, (a, rh, rw), (a, rl, rh, rw)
+    n = pp + h * w
+    trace = np.zeros((sh.layers + 1, n, sh.width), dtype=np.float32)
+    d._ck(E.lib().exn_test_trace(d.h, trace.ctypes.data, trace.size))
+    try:
+        d.velocity(ctx, p, lat, h, w, 1.0, ref=dref)
+    finally:
+        d._ck(E.lib().exn_test_trace(d.h, None, 0))
+    keep = ("time_text_embed.", "modulation.", "norm_out.") + tuple("transformer_blocks.%d." % i for i in blocks)
+    sw = O.SynthWeights.make(sh, seed=1, only=lambda name: name.startswith(keep))
+    _, pieces, _ = O.modulation(sw, sh, 1.0)
+    row = np.where(np.arange(n) < pp, 1, 0)
+    cos, sin = O.rope_tables(O.dit_positions(pp, h, w, refpos))
+    out = []
+    for il in blocks:
+        want = O.block(sw, sh, il, trace[il], pieces, row, cos, sin, pp, b0, b1)
+        out.append((il, O.rel_l2(trace[il + 1], want), O.rel_l2(trace[il + 1] - trace[il], want - trace[il])))
+    return out
+
+
 def test_full_blocks_match_oracle(full, inputs):
     """Per-block activations at full size, the tolerance's own terms: blocks 0, 15 and 31 of a
     sigma = 1 forward, each run by the fp32 oracle from the GPU's input to that block; rel-L2 <= 2e-2
     on the block's output and on its update (output - input)."""
-    sh = O.Shape()
     ctx, lat = inputs
-    n = P + H * W
-    trace = np.zeros((sh.layers + 1, n, sh.width), dtype=np.float32)
-    full._ck(E.lib().exn_test_trace(full.h, trace.ctypes.data, trace.size))
-    try:
-        full.velocity(ctx[0], P, lat[0], H, W, 1.0)
-    finally:
-        full._ck(E.lib().exn_test_trace(full.h, None, 0))
-    blocks = (0, 15, 31)
-    keep = ("time_text_embed.", "modulation.", "norm_out.") + tuple("transformer_blocks.%d." % i for i in blocks)
-    sw = O.SynthWeights.make(sh, seed=1, only=lambda name: name.startswith(keep))
-    _, pieces, _ = O.modulation(sw, sh, 1.0)
-    row = np.where(np.arange(n) < P, 1, 0)
-    cos, sin = O.rope_tables(O.dit_positions(P, H, W, None))
-    for il in blocks:
-        want = O.block(sw, sh, il, trace[il], pieces, row, cos, sin, P)
-        assert O.rel_l2(trace[il + 1], want) <= 2e-2, il
-        assert O.rel_l2(trace[il + 1] - trace[il], want - trace[il]) <= 2e-2, il
+    for il, r_out, r_upd in _blocks_vs_oracle(full, P, H, W, ctx[0], lat[0], (0, 15, 31)):
+        assert r_out <= 2e-2, (il, r_out)
+        assert r_upd <= 2e-2, (il, r_upd)
+
+
+def test_full_cfg3_blocks_match_oracle(full):
+    """BASELINE config 3 at full size: 1536 x 1024 (a 64 x 96 latent: the RoPE grid's centring
+    differs per axis, src/host.lisp:32-35) and 256 text rows, 6400 rows; blocks 0 and 31."""
+    p3, h3, w3 = 256, 64, 96
+    ctx, lat = O.synth_inputs(O.Shape(), p3, h3, w3, seed=0)
+    for il, r_out, r_upd in _blocks_vs_oracle(full, p3, h3, w3, ctx[0], lat[0], (0, 31)):
+        assert r_out <= 2e-2, (il, r_out)
+        assert r_upd <= 2e-2, (il, r_upd)
+
+
+def test_full_cfg4_edit_blocks_match_oracle(full):
+    """BASELINE config 4 at full size: an edit, 512 text rows with a 64 x 64 reference picture
+    after text row 8 (prefix 4608 rows, the reference's rows see their own block whole) and the
+    64 x 64 target: 8704 rows; blocks 0 and 31."""
+    p4, h4, w4, a4 = 512, 64, 64, 8
+    ctx, lat = O.synth_inputs(O.Shape(), p4, h4, w4, seed=0)
+    _, rl = O.synth_inputs(O.Shape(), 1, h4, w4, seed=4)
+    for il, r_out, r_upd in _blocks_vs_oracle(full, p4, h4, w4, ctx[0], lat[0], (0, 31), ref=(a4, rl[0])):
+        assert r_out <= 2e-2, (il, r_out)
+        assert r_upd <= 2e-2, (il, r_upd)
 
 
 def test_full_first_velocity_matches_ref_dit(full, inputs):

@@ -1,4 +1,4 @@
-"""Sequence parallelism (Ulysses) over 2 (and, where there are 4, 4) GPUs: the rows of one
+"""Sequence parallelism (Ulysses) over 2 (and, where there are 4 or 8, 4 and 8) GPUs: the rows of one
 picture split between the processes, Q/K/V and the attention output stored by the QKV GEMM and
 the attention kernel straight into the rank that keeps them (peer memory over NVLink).  Every
 row's arithmetic is the one-GPU arithmetic, so the result must equal a one-GPU handle's bit for
@@ -28,7 +28,8 @@ def _two_gpus():
 
 # world size -> (DiT shape, reference picture h, w): width / world a multiple of 256, and the
 # prefix (8 text rows + the reference's) and image (4 x 6) rows divisible by the world size
-CASES = {2: (SHAPE, 2, 3), 4: (dict(width=1024, layers=2, ffn=3072, context=512), 2, 2)}
+CASES = {2: (SHAPE, 2, 3), 4: (dict(width=1024, layers=2, ffn=3072, context=512), 2, 2),
+         8: (dict(width=2048, layers=2, ffn=6144, context=512), 2, 4)}
 
 
 def _rank(rank, world, uid, q):
@@ -54,7 +55,7 @@ def _rank(rank, world, uid, q):
         q.put((rank, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_sequence_parallel_equals_one_gpu(world):
     if _gpus() < world:
         pytest.skip("needs %d GPUs" % world)
