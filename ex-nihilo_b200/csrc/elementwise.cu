@@ -188,65 +188,191 @@ __global__ void k_temb(float* emb, double t, int freq) {
 }
 
 constexpr int GEMV_WARPS = 8;
-constexpr int GEMV_ROWS = 4;  // output rows per warp: x is staged once per block of 32 rows
 constexpr int GEMV_MAXM = 2;
+constexpr int GEMV_CHUNKS = 8;  // 16-byte weight loads a lane keeps in flight
 
-// y[m][o] = act(sum_k x[m][k] W[o][k]).  Each lane reads 16 contiguous
-// weight bytes (Q8_0: half a block, the block scale shared by a lane pair)
-// or 8 bf16 / 4+4 f32, so a warp streams 512 (256) weights of a row per step.
-template <int KIND>
-__global__ void __launch_bounds__(GEMV_WARPS * 32)
+// y[m][o] = act(sum_k x[m][k] W[o][k]), M <= 2: HBM-bound on W.  A warp owns
+// ROWS consecutive output rows; each lane reads 16 contiguous weight bytes a
+// chunk (Q8_0: half a block, the block scale shared by a lane pair; or 8
+// bf16 / 4+4 f32) and issues GEMV_CHUNKS of them before using any, so a warp
+// keeps 4 KB of the row in flight (the HBM latency is hidden by bytes in
+// flight, not by arithmetic).  x (M x in floats) is staged in shared memory
+// once per block, permuted so that the float4 j of a lane's chunk sits at
+// ((chunk * J + j) * 32 + lane), J = EPC / 4: the 32 lanes of a warp then
+// read 512 contiguous bytes per instruction (in x's own order a lane's 64
+// contiguous bytes would put 16 lanes on the same 4 banks).  A lane adds its
+// chunks in column order and the warp sum follows, so the result does not
+// depend on ROWS.
+template <int KIND, int RB>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2)
     k_gemv(const void* __restrict__ wv, const __half* __restrict__ wd, const float* __restrict__ x,
-           float* __restrict__ y, int m, int in, int out, int act, int piece) {
+           float* __restrict__ y, int m, int in, int out, int act, int piece, int rows) {
   extern __shared__ float4 xs4[];
-  const float* xs = reinterpret_cast<const float*>(xs4);
-  for (int i = threadIdx.x; i < m * in / 4; i += blockDim.x) xs4[i] = reinterpret_cast<const float4*>(x)[i];
+  constexpr int EPC = KIND == W_Q8 ? 16 : 8;  // weights a lane takes per chunk
+  constexpr int J = EPC / 4;                  // float4 of x per lane per chunk
+  const int row4 = (in + 32 * EPC - 1) / (32 * EPC) * 8 * EPC;  // float4 per row of x, whole chunks
+  {
+    // x into shared memory (permuted, above): consecutive threads fill consecutive float4 of
+    // the permuted layout (conflict-free stores) and gather x from L2, 8 loads in flight each
+    const int in4 = in / 4, n4 = m * row4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * blockDim.x) {
+      float4 t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * blockDim.x;
+        const int mm = i / row4, p = i - mm * row4;
+        const int ln = p & 31, cj = p >> 5, chunk = cj / J, jj = cj - chunk * J;
+        const int k4 = (chunk * 32 * EPC + ln * EPC) / 4 + jj;  // float4 index of x's row
+        t[j] = i < n4 && k4 < in4 ? __ldg(x4 + mm * in4 + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * blockDim.x;
+        if (i < n4) xs4[i] = t[j];
+      }
+    }
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int rr = 0; rr < GEMV_ROWS; ++rr) {
-    const int o = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS + rr;
-    if (o >= out) return;
-    float acc[GEMV_MAXM] = {0.f, 0.f};
-    if constexpr (KIND == W_Q8) {
-      const int8_t* q = static_cast<const int8_t*>(wv) + static_cast<long long>(o) * in;
-      const __half* d = wd + static_cast<long long>(o) * (in / 32);
-      for (int k0 = lane * 16; k0 < in; k0 += 512) {
-        const int4 qv = __ldg(reinterpret_cast<const int4*>(q + k0));
-        const float sc = __half2float(d[k0 >> 5]);
-        const int qw[4] = {qv.x, qv.y, qv.z, qv.w};
-        for (int mm = 0; mm < m; ++mm) {
-          const float4* xr = reinterpret_cast<const float4*>(xs + mm * in + k0);
-          float s = 0.f;
+  if constexpr (KIND == W_Q8) {
+    // RB rows at a time share each chunk of x read from shared memory; RB x CH = 8 16-byte
+    // loads per lane in flight
+    constexpr int CH = GEMV_CHUNKS / RB;
+    const int8_t* qbase = static_cast<const int8_t*>(wv);
+    for (int r0 = 0; r0 < rows; r0 += RB) {
+      const int o0 = (blockIdx.x * GEMV_WARPS + warp) * rows + r0;
+      if (o0 >= out) return;
+      float acc[RB][GEMV_MAXM];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float4 xv = xr[k];
-            const int w4 = qw[k];
-            s += static_cast<float>(static_cast<int8_t>(w4 & 0xFF)) * xv.x;
-            s += static_cast<float>(static_cast<int8_t>((w4 >> 8) & 0xFF)) * xv.y;
-            s += static_cast<float>(static_cast<int8_t>((w4 >> 16) & 0xFF)) * xv.z;
-            s += static_cast<float>(static_cast<int8_t>(w4 >> 24)) * xv.w;
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int mm = 0; mm < GEMV_MAXM; ++mm) acc[r][mm] = 0.f;
+      for (int kb = 0; kb < in; kb += 32 * EPC * CH) {
+        int4 qv[RB][CH];
+        float sc[RB][CH];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          const bool rv = r0 + r < rows && o0 + r < out;
+          const long long o = o0 + r;
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const int k0 = kb + c * 32 * EPC + lane * EPC;
+            const bool v = rv && k0 < in;
+            qv[r][c] = v ? __ldg(reinterpret_cast<const int4*>(qbase + o * in + k0)) : make_int4(0, 0, 0, 0);
+            sc[r][c] = v ? __half2float(wd[o * (in / 32) + (k0 >> 5)]) : 0.f;
           }
-          acc[mm] += sc * s;
+        }
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int k0 = kb + c * 32 * EPC + lane * EPC;
+          if (k0 >= in) break;
+          const float4* xc = xs4 + ((kb / (32 * EPC) + c) * J) * 32 + lane;  // this lane's chunk of x row 0
+          float4 xv[GEMV_MAXM][4];
+#pragma unroll
+          for (int mm = 0; mm < GEMV_MAXM; ++mm)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) xv[mm][k] = mm < m ? xc[mm * row4 + k * 32] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const int qw[4] = {qv[r][c].x, qv[r][c].y, qv[r][c].z, qv[r][c].w};
+            // int8 -> float exactly without the conversion unit: with its sign bit flipped a byte
+            // is q + 128 in 0..255; placed as the low mantissa byte of 2^23 (0x4B000000) it reads
+            // as the float 2^23 + q + 128, and subtracting 2^23 + 128 leaves q
+            float wf[16];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t u = static_cast<uint32_t>(qw[k]) ^ 0x80808080u;
+              wf[4 * k] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.f;
+              wf[4 * k + 1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.f;
+              wf[4 * k + 2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.f;
+              wf[4 * k + 3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.f;
+            }
+#pragma unroll
+            for (int mm = 0; mm < GEMV_MAXM; ++mm) {
+              if (mm < m) {
+                float s = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  s += wf[4 * k] * xv[mm][k].x;
+                  s += wf[4 * k + 1] * xv[mm][k].y;
+                  s += wf[4 * k + 2] * xv[mm][k].z;
+                  s += wf[4 * k + 3] * xv[mm][k].w;
+                }
+                acc[r][mm] += sc[r][c] * s;
+              }
+            }
+          }
         }
       }
-    } else {
-      for (int k0 = lane * 8; k0 < in; k0 += 256) {
-        float wf[8];
-        if constexpr (KIND == W_BF16) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(wv) + static_cast<long long>(o) * in + k0));
-          const bf16* bp = reinterpret_cast<const bf16*>(&u);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) wf[e] = __bfloat162float(bp[e]);
-        } else {
-          const float4* fp = reinterpret_cast<const float4*>(static_cast<const float*>(wv) + static_cast<long long>(o) * in + k0);
-          const float4 a = __ldg(fp), b = __ldg(fp + 1);
-          wf[0] = a.x; wf[1] = a.y; wf[2] = a.z; wf[3] = a.w; wf[4] = b.x; wf[5] = b.y; wf[6] = b.z; wf[7] = b.w;
+      for (int r = 0; r < RB; ++r) {
+        if (r0 + r >= rows || o0 + r >= out) break;
+        const int o = o0 + r;
+#pragma unroll
+        for (int mm = 0; mm < GEMV_MAXM; ++mm) {
+          if (mm >= m) break;
+          float v = warp_sum(acc[r][mm]);
+          if (lane == 0) {
+            if (act == 1) v = v / (1.f + expf(-v));
+            if (act == 2) {
+              const int pc = o / piece;
+              if (pc == 1 || pc == 3) v = tanhf(v);
+            }
+            y[static_cast<long long>(mm) * out + o] = v;
+          }
         }
-        for (int mm = 0; mm < m; ++mm) {
-          float s = 0.f;
+      }
+    }
+  } else {
+  for (int rr = 0; rr < rows; ++rr) {
+    const int o = (blockIdx.x * GEMV_WARPS + warp) * rows + rr;
+    if (o >= out) return;
+    float acc[GEMV_MAXM] = {0.f, 0.f};
+    for (int kb = 0; kb < in; kb += 32 * EPC * GEMV_CHUNKS) {
+      {
+        uint4 raw[GEMV_CHUNKS][KIND == W_F32 ? 2 : 1];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) s += wf[e] * xs[mm * in + k0 + e];
-          acc[mm] += s;
+        for (int c = 0; c < GEMV_CHUNKS; ++c) {
+          const int k0 = kb + c * 32 * EPC + lane * EPC;
+          if constexpr (KIND == W_BF16) {
+            raw[c][0] = k0 < in ? __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(wv) +
+                                                                      static_cast<long long>(o) * in + k0))
+                                : make_uint4(0, 0, 0, 0);
+          } else {
+            const uint4* fp =
+                reinterpret_cast<const uint4*>(static_cast<const float*>(wv) + static_cast<long long>(o) * in + k0);
+            raw[c][0] = k0 < in ? __ldg(fp) : make_uint4(0, 0, 0, 0);
+            raw[c][KIND == W_F32 ? 1 : 0] = k0 < in ? __ldg(fp + 1) : make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < GEMV_CHUNKS; ++c) {
+          const int k0 = kb + c * 32 * EPC + lane * EPC;
+          if (k0 >= in) break;
+          float wf[8];
+          if constexpr (KIND == W_BF16) {
+            const bf16* bp = reinterpret_cast<const bf16*>(&raw[c][0]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) wf[e] = __bfloat162float(bp[e]);
+          } else {
+            const float* f0 = reinterpret_cast<const float*>(&raw[c][0]);
+            const float* f1 = reinterpret_cast<const float*>(&raw[c][KIND == W_F32 ? 1 : 0]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              wf[e] = f0[e];
+              wf[4 + e] = f1[e];
+            }
+          }
+          const float4* xc = xs4 + ((kb / (32 * EPC) + c) * J) * 32 + lane;
+          for (int mm = 0; mm < m; ++mm) {
+            const float4 xa = xc[mm * row4], xb = xc[mm * row4 + 32];
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s += wf[e] * xv[e];
+            acc[mm] += s;
+          }
         }
       }
     }
@@ -261,6 +387,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32)
         y[static_cast<long long>(mm) * out + o] = v;
       }
     }
+  }
   }
 }
 
@@ -433,14 +560,20 @@ void temb_launch(float* emb, double sigma, int freq, cudaStream_t st) {
 
 void gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out, int act,
                  int piece, cudaStream_t st) {
-  const unsigned grid = blocks_for(out, GEMV_WARPS * GEMV_ROWS);
-  const size_t sm = static_cast<size_t>(m) * in * sizeof(float);
-  if (kind == W_Q8)
-    k_gemv<W_Q8><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece);
+  // rows a warp owns: 4 (a group of rows sharing each x read) when that still leaves >= 2 blocks
+  // per SM of a 148-SM part, else 1 (x is staged once a block)
+  const int rows = blocks_for(out, GEMV_WARPS * 4) >= 2 * 148 ? 4 : 1;
+  const unsigned grid = blocks_for(out, GEMV_WARPS * rows);
+  const int epc = kind == W_Q8 ? 16 : 8;  // x is staged in whole chunks of 32 lanes x epc floats
+  const size_t sm = static_cast<size_t>(m) * ((in + 32 * epc - 1) / (32 * epc)) * (32 * epc) * sizeof(float);
+  if (kind == W_Q8 && rows == 4)
+    k_gemv<W_Q8, 4><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
+  else if (kind == W_Q8)
+    k_gemv<W_Q8, 1><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
   else if (kind == W_BF16)
-    k_gemv<W_BF16><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece);
+    k_gemv<W_BF16, 1><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
   else
-    k_gemv<W_F32><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece);
+    k_gemv<W_F32, 1><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
 }
 
 void q8_raw_to_bf16_launch(const uint8_t* raw, bf16* dst, long long rows, int cols, long long row0, int ilv,
