@@ -1789,6 +1789,16 @@ int exn_test_profile(exn_handle* h, int on) {
 
 long long exn_test_launch_count(const exn_handle* h) { return h ? h->launches : -1; }
 
+int exn_test_wait_probe(exn_handle* h, double seconds) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_wait_probe: null handle");
+  if (!(seconds > 0.0) || seconds > 1.0) return fail(h, EXN_EINVAL, "exn_test_wait_probe: %g s (0 < s <= 1)", seconds);
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  wait_probe_launch(h->d_status, static_cast<unsigned long long>(seconds * 1e9), h->st);
+  CK(cudaGetLastError());
+  return check_status(h);
+}
+
 int exn_test_last_call_ms(const exn_handle* h, double* ms) {
   if (!h || !ms) return EXN_EINVAL;
   *ms = h->last_call_ms;

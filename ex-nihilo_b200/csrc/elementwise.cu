@@ -391,6 +391,21 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2)
   }
 }
 
+// One CTA waits, through the pipelines' own bounded wait, on an mbarrier that nothing arrives
+// on: after LIMIT_NS the wait gives up, sets STATUS_TIMEOUT_PROBE and the kernel returns.  It
+// shows on a GPU that a stalled pipeline ends in a status the host reads, not in a hang.
+__global__ void k_wait_probe(int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, STATUS_TIMEOUT_PROBE, limit_ns);
+}
+
 // destination row of weight row r: gate_up interleaved by 128 when ilv (= FFN) > 0
 __device__ __forceinline__ long long dst_row(long long r, long long row0, int ilv) {
   if (ilv <= 0) return row0 + r;
@@ -608,6 +623,10 @@ void f16_to_f32_launch(const __half* src, float* dst, long long n, cudaStream_t 
 
 void bf16_to_f32_launch(const bf16* src, float* dst, long long n, cudaStream_t st) {
   k_bf16_to_f32<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, n);
+}
+
+void wait_probe_launch(int* status, unsigned long long limit_ns, cudaStream_t st) {
+  k_wait_probe<<<1, 32, 0, st>>>(status, limit_ns);
 }
 
 void add_scalar_launch(float* v, long long n, float a, cudaStream_t st) {

@@ -25,6 +25,7 @@ enum : int {
   STATUS_TIMEOUT_GEMM = 1,
   STATUS_TIMEOUT_ATTN = 2,
   STATUS_BAD_ARG = 4,
+  STATUS_TIMEOUT_PROBE = 8,  // the test kernel whose wait is meant to run out
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -84,16 +85,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for the phase of parity PARITY to complete.  False when the CTA gave
-// up: another role already aborted, or this wait ran past EXN_WAIT_NS (then
-// it raises the abort flag and ORs CODE into *status).
+// up: another role already aborted, or this wait ran past LIMIT_NS (then it
+// raises the abort flag and ORs CODE into *status).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          int* status, int code, uint64_t limit_ns = EXN_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > EXN_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicOr(status, code);
       return false;

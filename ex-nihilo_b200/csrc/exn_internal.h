@@ -158,5 +158,7 @@ void synth_f32_launch(float* v, long long n, uint64_t seed, uint32_t stream, flo
 void q8_to_bf16_launch(const int8_t* qs, const __half* d, bf16* dst, long long rows, int cols, long long row0,
                        int ilv, cudaStream_t st);
 void add_scalar_launch(float* v, long long n, float a, cudaStream_t st);
+// one CTA whose bounded wait on an mbarrier nothing arrives on runs out after LIMIT_NS
+void wait_probe_launch(int* status, unsigned long long limit_ns, cudaStream_t st);
 
 }  // namespace exn

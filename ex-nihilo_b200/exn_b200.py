@@ -106,6 +106,7 @@ def lib():
         "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_launch_count": (ctypes.c_longlong, [H]),
         "exn_test_last_call_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
+        "exn_test_wait_probe": (ctypes.c_int, [H, ctypes.c_double]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(L, name)

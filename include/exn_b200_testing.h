@@ -54,6 +54,13 @@ int exn_test_profile(exn_handle* h, int on);
 /* Kernels of this library the handle has queued since it was opened. */
 long long exn_test_launch_count(const exn_handle* h);
 
+/* Failure detection on the GPU without a fault: one CTA waits, through the
+ * kernels' own bounded mbarrier wait, on a barrier nothing arrives on, with a
+ * limit of SECONDS (0 < SECONDS <= 1).  The wait runs out, the kernel records
+ * it in the handle's status word and returns; the call returns EXN_ETIMEOUT
+ * as a stalled pipeline would, and the handle stays usable. */
+int exn_test_wait_probe(exn_handle* h, double seconds);
+
 /* Device time in ms (CUDA events on the handle's stream) of the last
  * successful exn_velocity / exn_generate: from the end of the inputs' upload
  * to the start of the result's download, so the DiT forwards (and, across

@@ -144,3 +144,23 @@ def test_qkv_epilogue_norm_rope(dit):
         got = out.float().cpu().numpy()
         maxrel = np.abs(got - want).max() / np.abs(want).max()
         assert maxrel < 2 ** -7, (name, maxrel)
+
+
+def test_a_wait_that_runs_out_ends_in_a_timeout_status(dit):
+    # failure detection without a GPU fault: a CTA waits, through the kernels' own bounded
+    # mbarrier wait, on a barrier nothing arrives on (limit 50 ms); the call returns EXN_ETIMEOUT
+    # with the kernels' message, and the handle works afterwards
+    import time
+    t0 = time.perf_counter()
+    rc = E.lib().exn_test_wait_probe(dit.h, 0.05)
+    dt = time.perf_counter() - t0
+    assert rc == 6, rc                                  # EXN_ETIMEOUT
+    assert b"gave up waiting" in E.lib().exn_last_error(dit.h)
+    assert 0.04 < dt < 10.0, dt
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(128, 256, generator=g).to(torch.bfloat16).cuda()
+    b = (torch.randn(256, 256, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    c = torch.full((128, 256), float("nan"), dtype=torch.float32, device="cuda")
+    dit._ck(E.lib().exn_test_gemm(dit.h, a.data_ptr(), b.data_ptr(), c.data_ptr(), 128, 256, 256))
+    ref = a.double() @ b.double().T
+    assert (c.double() - ref).abs().max().item() / ref.abs().max().item() < 1e-5
