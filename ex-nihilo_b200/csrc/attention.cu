@@ -11,7 +11,9 @@
 // src/cuda-dit.lisp:207-218).
 //
 // One CTA = one (sample, head) and two tiles of 128 queries (a, b) that
-// share every K/V tile.  Keys are taken 64 at a time ("units"; K and V are
+// share every K/V tile; when the last round of such pair items would fill at
+// most half the SMs, each of its items runs as two CTAs of one tile (no
+// ping-pong partner; the same per-row arithmetic).  Keys are taken 64 at a time ("units"; K and V are
 // loaded 128 keys at a time, two units a load):
 //   warp 0      TMA: Q_a, Q_b once; K_t, V_t (128 keys x 128 dims, bf16)
 //               through a ring of 4 slots
@@ -82,15 +84,26 @@ struct Bars {
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
-                int b0, int b1, int width, float scale_log2, const SpOut spo, int* status) {
+                int b0, int b1, int width, float scale_log2, int qpairs, int heads, int n_pairs, const SpOut spo,
+                int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, head = blockIdx.y, sample = blockIdx.z;
-  const int qlast = min(nq, (qt + 1) * 2 * TILE) - 1;
+  // work item: blocks below N_PAIRS take a pair of query tiles (a, b); each later block takes one
+  // tile of a pair item (the last round of pair items split in two when that fills the SMs better)
+  int item = blockIdx.x, tiles = 2, tile0 = 0;
+  if (item >= n_pairs) {
+    const int sgl = item - n_pairs;
+    item = n_pairs + (sgl >> 1);
+    tiles = 1;
+    tile0 = sgl & 1;
+  }
+  const int qt = item % qpairs, head = (item / qpairs) % heads, sample = item / (qpairs * heads);
+  const int qbase = qt * 2 * TILE + tile0 * TILE;  // first query row (within the pass) of tile a
+  const int qlast = min(nq, qbase + tiles * TILE) - 1;
   const int last_key = xa_lim(q0 + qlast, p, l, b0, b1);
   const int nunits = last_key / UNIT + 1;   // 64-key units any row of the CTA sees
   const int nloads = (nunits + 1) / 2;      // 128-key K/V loads
@@ -99,7 +112,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(&bars->q_full, 1);
     for (int i = 0; i < SLOTS; ++i) {
       mbar_init(&bars->slot_full[i], 1);
-      mbar_init(&bars->slot_empty[i], 2);  // a K or V tile is free once both tiles' MMAs are done with it
+      mbar_init(&bars->slot_empty[i], tiles);  // a K or V tile is free once every tile's MMAs are done with it
     }
     for (int x = 0; x < 2; ++x) {
       for (int b = 0; b < 2; ++b) {
@@ -131,11 +144,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tma_prefetch(&tmV);
       griddep_wait();  // Q, K and V are the previous kernel's output
       const int hx = head * 128;
-      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
-      for (int x = 0; x < 2; ++x)
+      mbar_arrive_expect_tx(&bars->q_full, tiles * TILE_BYTES);
+      for (int x = 0; x < tiles; ++x)
         for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem + (x ? OFF_QB : OFF_QA) + hf * HALF, &tmQ, &bars->q_full, hx + hf * 64,
-                      qt * 2 * TILE + x * TILE, sample);
+          tma_load_3d(smem + (x ? OFF_QB : OFF_QA) + hf * HALF, &tmQ, &bars->q_full, hx + hf * 64, qbase + x * TILE,
+                      sample);
       // load number t: K_{t/2} for even t, V_{t/2} for odd t; slot t % SLOTS, its (t / SLOTS)-th use
       int issued = 0;
       for (int t = 0; t < 2 * nloads; ++t) {
@@ -157,7 +170,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
     }
   } else if (warp <= 2) {
-    if (lane == 0) {
+    if (lane == 0 && warp - 1 < tiles) {
       // ---- the MMAs of tile x.  This thread shares its scheduler with two busy softmax warps, so
       // its instruction stream is kept short: descriptors are formed once, as 32-bit low words
       // over a common high word (every operand here is 128B-swizzled with 1024-byte 8-row
@@ -223,12 +236,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       volatile int no_abort = 0;
       mbar_wait(&bars->done[x], 0, &no_abort, nullptr, 0);
     }
-  } else {
+  } else if ((warp - 3) >> 2 < tiles) {
     // ---- softmax: tile x, TMEM lane quarter wq, query row r of the tile
     const int x = (warp - 3) >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
-    const int qi = qt * 2 * TILE + x * TILE + r;  // query index within the pass
+    const int qi = qbase + x * TILE + r;  // query index within the pass
     const int lim = xa_lim(q0 + qi, p, l, b0, b1);
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + x * 128;
@@ -244,7 +257,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     // partner is left waiting at a barrier.
     const uint32_t my_turn = (x ? 5u : 1u) + static_cast<uint32_t>(wq);
     const uint32_t other_turn = (x ? 1u : 5u) + static_cast<uint32_t>(wq);
-    if (x == 1) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");  // tile a goes first
+    const bool pingpong = tiles == 2;  // a lone tile has the schedulers' MUFU pipes to itself
+    if (pingpong && x == 1) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");  // tile a goes first
     for (int u = 0; u < nunits; ++u) {
       const int b = u & 1;
       // the warp stays converged through the whole loop (warp-uniform waits and branches), so
@@ -302,7 +316,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           }
         }
       }
-      asm volatile("bar.sync %0, 64;" ::"r"(my_turn) : "memory");
+      if (pingpong) asm volatile("bar.sync %0, 64;" ::"r"(my_turn) : "memory");
       uint32_t pk[UNIT / 2];  // P as bf16 pairs: key 2c and 2c+1 in column c
       if (ok) {
         // x = s * scale - m and the row sums on paired f32 instructions (two keys per issue)
@@ -323,7 +337,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         f2_split(fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3])), a0, a1);
         lsum += a0 + a1;
       }
-      if (x == 0 || u + 1 < nunits) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");
+      if (pingpong && (x == 0 || u + 1 < nunits)) asm volatile("bar.arrive %0, 64;" ::"r"(other_turn) : "memory");
       if (ok) {
         tmem_st32_conv(s_addr + b * UNIT, pk);
         tmem_st_wait();
@@ -395,7 +409,26 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   if (make_tmap_bf16(&tq, a.q, 3, dq, sq, box) || make_tmap_bf16(&tk, a.k, 3, dk, sk, box) ||
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
-  dim3 grid((a.nq + 2 * TILE - 1) / (2 * TILE), a.heads, a.batch);
+  // pair items (two query tiles a CTA); when the last round of them fills at most half the SMs,
+  // its items run as two one-tile CTAs each (EXN_ATT_SINGLE=0: pairs only, 1: every item split)
+  const int qpairs = (a.nq + 2 * TILE - 1) / (2 * TILE);
+  const int items = qpairs * a.heads * a.batch;
+  static int sms = 0, mode = -1;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const char* e = getenv("EXN_ATT_SINGLE");
+    mode = e ? atoi(e) : 2;
+  }
+  int n_pairs = items;
+  if (mode == 1) {
+    n_pairs = 0;
+  } else if (mode == 2 && sms > 0) {
+    const int last = items % sms;
+    if (last > 0 && 2 * last <= sms) n_pairs = items - last;
+  }
+  const dim3 grid(static_cast<unsigned>(n_pairs + 2 * (items - n_pairs)));
   SpOut spo;
   for (int i = 0; i < kMaxSp; ++i) spo.out[i] = a.sp_out[i];
   spo.ld = a.sp_ld;
@@ -406,7 +439,8 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   spo.img0 = a.sp_img0;
   if (spo.out[0] != nullptr && (a.batch != 1 || spo.nl <= 0 || (spo.img0 > 0 && spo.pl <= 0))) return -1;
   return static_cast<int>(launch_pdl(k_attention, grid, dim3(ATT_THREADS), ATT_SMEM, st, tq, tk, tv, a.out, a.nq, a.q0,
-                                     a.p, a.l, a.b0, a.b1, a.width, a.scale_log2, spo, d_status));
+                                     a.p, a.l, a.b0, a.b1, a.width, a.scale_log2, qpairs, a.heads, n_pairs, spo,
+                                     d_status));
 }
 
 }  // namespace exn
