@@ -125,10 +125,13 @@ def run_case(R, name, case, outdir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-dir", default=os.environ.get("EXN_REF_INSPECT", "/root/reference/inspect"))
+    ap.add_argument("--ref-dir", default=os.environ.get("EXN_REF_INSPECT"),
+                    help="the reference tree's inspect/ directory (holds ref_dit.py); or set EXN_REF_INSPECT")
     ap.add_argument("--full", action="store_true", help="also the full D=4096 8-step case (tens of minutes)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.ref_dir:
+        ap.error("--ref-dir (or EXN_REF_INSPECT) is required: the reference's inspect/ directory")
     R = load_ref(args.ref_dir)
     cases = dict(CASES)
     if args.full:
