@@ -157,7 +157,7 @@ def test_batch_equals_single(tiny):
         assert O.rel_l2(zb[i], zi) < 1e-6, i
 
 
-@pytest.mark.parametrize("mtype", ["q8_0", "f32", "bf16"])
+@pytest.mark.parametrize("mtype", ["q8_0", "f32", "bf16", "f16"])
 def test_gguf_upload_equals_synthetic(tmp_path, tiny, tiny_sw, mtype):
     path = tmp_path / "dit.gguf"
     write_gguf(path, tiny_sw, matrix_type=mtype)
@@ -173,7 +173,7 @@ def test_gguf_upload_equals_synthetic(tmp_path, tiny, tiny_sw, mtype):
     v0 = tiny.velocity(ctx[0], p, lat[0], h, w, 0.5)
     if mtype == "q8_0":
         assert O.rel_l2(v, v0) < 1e-6
-    else:   # the GEMV matrices keep f32 / bf16 values
+    else:   # the GEMV matrices keep f32 / bf16 / f16 values
         assert O.rel_l2(v, v0) < 1e-2
 
 
