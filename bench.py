@@ -44,6 +44,10 @@ SIGMAS = (1.0, 0.978453, 0.95418, 0.926626, 0.89508, 0.845148, 0.704534, 0.41456
 W, LAYERS, FFN, CTX, LAT, FREQ, HEADS = 4096, 32, 12288, 4096, 64, 256, 32
 P, H, WW = 128, 64, 64
 PUBLISHED_IMAGES_PER_S = 1.0 / 9.5   # README.md:92-93: the 8 DiT steps of a 1024^2 picture in ~9.5 s (RTX 3090)
+# DRAM bytes (read + write) of one gate_up + SwiGLU launch at 4224 rows, from an ncu capture, and the
+# algorithmic bytes of that launch: A 4224 x 4096 + B 24576 x 4096 bf16 read, 4224 x 12288 bf16 written
+GATEUP_TRAFFIC = 347.7e6
+GATEUP_ALG_BYTES = 2.0 * (4224 * 4096 + 24576 * 4096 + 4224 * 12288)
 
 
 # --------------------------------------------------------------------------- algorithmic work
@@ -240,6 +244,16 @@ def barrier(dist):
         torch.cuda.synchronize()
 
 
+def cfg2_config(world, batch):
+    """The workload keys both arms report for BASELINE config 2."""
+    return {"workload": "BASELINE config 2: 1024^2 picture (64x64 latent) + 128 text rows, 8 Euler steps",
+            "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks, FFN 12288", "global_batch": world * batch,
+            "batch_per_gpu": batch, "seq_len": P + H * WW, "parallelism": "dp%d (replicas)" % world,
+            "accumulate": "fp32", "residual": "fp32",
+            "l2": "each picture streams 14 GB of bf16 weights (> 126 MB L2)",
+            "vs_baseline_ref": "RTX 3090, 8 DiT steps ~9.5 s (README.md:92-93)"}
+
+
 def run_exn(args):
     import torch
     import exn_b200 as E
@@ -351,12 +365,7 @@ def run_exn(args):
         "dtype": "bf16",
         "data": "synthetic: random-init Q8_0 weights (seed 1, dequantised once to bf16 in HBM); contexts and "
                 "noise ~N(0,1) from the oracle's generator",
-        "config": {"workload": "BASELINE config 2: 1024^2 picture (64x64 latent) + 128 text rows, 8 Euler steps",
-                   "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks, FFN 12288", "global_batch": world * B,
-                   "batch_per_gpu": B, "seq_len": P + H * WW, "parallelism": "dp%d (replicas)" % world,
-                   "accumulate": "fp32", "residual": "fp32",
-                   "l2": "each picture streams 14 GB of bf16 weights (> 126 MB L2)",
-                   "vs_baseline_ref": "RTX 3090, 8 DiT steps ~9.5 s (README.md:92-93)"},
+        "config": cfg2_config(world, B),
         "steps_per_s": round(8 * value, 3),
         "tc_peak_frac": round(value / world * sum(picture_flops(1, args.layers)) / 1e12 / bt, 4),
         "tc_peak_frac_of_burst": round(value / world * sum(picture_flops(1, args.layers)) / 1e12 / bt_burst, 4),
@@ -368,9 +377,9 @@ def run_exn(args):
                                "largest kernel, 32% of a picture's kernel time)",
                      "achieved": round(gu_tflops, 1) if gu_tflops else None, "peak": bt, "unit": "TFLOP/s",
                      "frac": round(gu_tflops / bt, 4) if gu_tflops else None,
-                     "traffic": 347.7e6,
-                     "traffic_note": "dram read+write bytes of one launch at the first step's 4224 rows (ncu, "
-                                     "profiles/gemm2_swiglu_cfg2_first_step.md); algorithmic bytes 339.7e6",
+                     "traffic": GATEUP_TRAFFIC,
+                     "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at the first "
+                                     "step's 4224 rows; algorithmic bytes %.4g" % GATEUP_ALG_BYTES,
                      "algorithmic_flop_per_launch": 2.0 * (P + H * WW) * 2 * FFN * W,
                      "peak_source": src + " (MEASURED_PEAKS.json bf16_tflops_sustained: the kernels run inside a "
                                           "seconds-long step at the power cap; burst figure %.1f)" % bt_burst,
@@ -481,14 +490,20 @@ def run_reference(args):
                 times.append(cpu_picture_seconds(bs))
     sec = statistics.mean(times)
     v = 1.0 / sec
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    timed_s = sum(times) / cpu_picture_seconds(1.0)      # the block passes actually run in the timed steps
     return {
         "impl": "reference",
-        "metric": METRIC, "value": round(v, 6), "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps,
+        "metric": METRIC, "value": round(v, 6), "unit": "images/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": round(v / PUBLISHED_IMAGES_PER_S, 4), "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2: 1024^2 picture + 128 text rows, 8 Euler steps",
-                   "model": "Qwen-Image-2.1 DiT, D=4096, 32 blocks", "global_batch": 1, "seq_len": P + H * WW,
-                   "parallelism": "host CPU"},
+        "config": dict(cfg2_config(world, args.batch), parallelism="host CPU (rank 0 alone)"),
+        "extrapolated": True,
+        "timed_unit": "one DiT block",
+        "timed_s": round(timed_s, 2),
+        "extrapolation": "each step times one DiT block at the cached-step size (4096 rows x 4224 keys) and scales "
+                         "it by the %.1f block passes of a picture; ms_per_step is that estimate, not a measured "
+                         "picture" % cpu_picture_seconds(1.0),
         "cpu_baseline": {"value": round(v, 6), "unit": "images/s", "cores": threads, "kind": "port",
                          "sample": "each step one DiT block at 1024^2 (numpy oracle restating inspect/ref_dit.py; the "
                                    "reference's own ref_dit.py cannot travel to this box), scaled to a picture"},

@@ -35,8 +35,6 @@
 // is reachable only from warps w with w % 4 == q), which leave an issuing
 // thread few issue slots; one MMA thread per tile, on two schedulers, halves
 // the instructions each must get through.
-#include <stdlib.h>
-
 #include "exn_device.cuh"
 #include "exn_internal.h"
 
@@ -390,15 +388,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
 }
 
+// The attention kernel's dynamic shared-memory limit, raised on the CURRENT device (a per-device
+// attribute: each handle's device gets it at exn_open).
+int attention_prepare() {
+  return static_cast<int>(
+      cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM));
+}
+
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   if (a.nq <= 0 || a.l <= 0 || a.width % 128 || a.heads * 128 != a.width || a.kv_rows < a.l) return -1;
   if (a.q0 + a.nq > a.l) return -1;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess)
-      return -3;
-    attr_set = true;
-  }
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, TILE, 1};
   const uint64_t dq[3] = {static_cast<uint64_t>(a.width), static_cast<uint64_t>(a.nq),
@@ -410,23 +409,15 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
   // pair items (two query tiles a CTA); when the last round of them fills at most half the SMs,
-  // its items run as two one-tile CTAs each (EXN_ATT_SINGLE=0: pairs only, 1: every item split)
+  // its items run as two one-tile CTAs each (split_mode 0: pairs only, 1: every item split)
   const int qpairs = (a.nq + 2 * TILE - 1) / (2 * TILE);
   const int items = qpairs * a.heads * a.batch;
-  static int sms = 0, mode = -1;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const char* e = getenv("EXN_ATT_SINGLE");
-    mode = e ? atoi(e) : 2;
-  }
   int n_pairs = items;
-  if (mode == 1) {
+  if (a.split_mode == 1) {
     n_pairs = 0;
-  } else if (mode == 2 && sms > 0) {
-    const int last = items % sms;
-    if (last > 0 && 2 * last <= sms) n_pairs = items - last;
+  } else if (a.split_mode == 2 && a.sms > 0) {
+    const int last = items % a.sms;
+    if (last > 0 && 2 * last <= a.sms) n_pairs = items - last;
   }
   const dim3 grid(static_cast<unsigned>(n_pairs + 2 * (items - n_pairs)));
   SpOut spo;

@@ -172,6 +172,9 @@ struct SpBufs {
 struct exn_handle {
   exn_config cfg{};
   int sms = 0;
+  // attention work split (AttnArgs::split_mode, EXN_ATT_SINGLE at open) and the SM count it plans
+  // for (0: the device's); a testing entry point may change both
+  int att_mode = 2, att_sms = 0;
   cudaStream_t st = nullptr;
   std::string err;
   int* d_status = nullptr;
@@ -567,6 +570,20 @@ int gemm(exn_handle* h, const bf16* a, long long lda, const bf16* b, long long l
   return EXN_OK;
 }
 
+// emb(1000 sigma), emb(0) -> linear_1, SiLU -> linear_2, SiLU -> modulation (gates tanh'd) and
+// norm_out (row 0 only): src/cuda-dit.lisp:157-167
+int timestep_chain(exn_handle* h, double sigma) {
+  const exn_config& c = h->cfg;
+  const int W = c.width;
+  temb_launch(h->emb, sigma, c.freq, h->st);
+  int r = gemv_launch(h->lin1.kind, h->lin1.w, h->lin1.d, h->emb, h->e1, 2, c.freq, W, 1, 0, h->st);
+  if (!r) r = gemv_launch(h->lin2.kind, h->lin2.w, h->lin2.d, h->e1, h->e2, 2, W, W, 1, 0, h->st);
+  if (!r) r = gemv_launch(h->mod.kind, h->mod.w, h->mod.d, h->e2, h->modv, 2, W, 4 * W, 2, W, h->st);
+  if (!r) r = gemv_launch(h->nout.kind, h->nout.w, h->nout.d, h->e2, h->sc, 1, W, W, 0, 0, h->st);
+  if (r) return fail(h, EXN_ECUDA, "timestep GEMV launch failed: %d", r);
+  return EXN_OK;
+}
+
 int run_step(exn_handle* h, const StepIn& in) {
   const exn_config& c = h->cfg;
   // kernels this step queues (timestep 5, inputs 2 or 5 (+2 with a reference), RoPE 1, 7 a block, final 2)
@@ -582,11 +599,7 @@ int run_step(exn_handle* h, const StepIn& in) {
 
   prof_mark(h, 2);
   // timestep: emb(t), emb(0) -> linear_1, SiLU -> linear_2, SiLU -> modulation (gates tanh'd), norm_out (row 0)
-  temb_launch(h->emb, in.sigma, c.freq, h->st);
-  gemv_launch(h->lin1.kind, h->lin1.w, h->lin1.d, h->emb, h->e1, 2, c.freq, W, 1, 0, h->st);
-  gemv_launch(h->lin2.kind, h->lin2.w, h->lin2.d, h->e1, h->e2, 2, W, W, 1, 0, h->st);
-  gemv_launch(h->mod.kind, h->mod.w, h->mod.d, h->e2, h->modv, 2, W, 4 * W, 2, W, h->st);
-  gemv_launch(h->nout.kind, h->nout.w, h->nout.d, h->e2, h->sc, 1, W, W, 0, 0, h->st);
+  if ((rc = timestep_chain(h, in.sigma))) return rc;
   // the prompt (and an edit's picture) through txt_in / img_in, first pass only
   if (!in.cached && in.ptext > 0) {
     rms_launch(in.ctx, h->txt_norm, h->ctxn, B * in.ptext, c.context, h->st);
@@ -686,6 +699,8 @@ int run_step(exn_handle* h, const StepIn& in) {
     aa.width = W;
     aa.kv_rows = h->kv_l;
     aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    aa.sms = h->att_sms ? h->att_sms : h->sms;
+    aa.split_mode = h->att_mode;
     if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
     prof_mark(h, 0);
     GemmEpi eo;
@@ -924,11 +939,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
   h->launches += 5 + 3 + 7LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
 
   // timestep
-  temb_launch(h->emb, in.sigma, c.freq, h->st);
-  gemv_launch(h->lin1.kind, h->lin1.w, h->lin1.d, h->emb, h->e1, 2, c.freq, W, 1, 0, h->st);
-  gemv_launch(h->lin2.kind, h->lin2.w, h->lin2.d, h->e1, h->e2, 2, W, W, 1, 0, h->st);
-  gemv_launch(h->mod.kind, h->mod.w, h->mod.d, h->e2, h->modv, 2, W, 4 * W, 2, W, h->st);
-  gemv_launch(h->nout.kind, h->nout.w, h->nout.d, h->e2, h->sc, 1, W, W, 0, 0, h->st);
+  if ((rc = timestep_chain(h, in.sigma))) return rc;
   // first pass: every prefix row through txt_in (and an edit's picture through img_in), this rank's slice kept
   if (!in.cached) {
     if (in.ptext > 0) {
@@ -1012,6 +1023,8 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     aa.width = Wg;
     aa.kv_rows = b.kv_l;
     aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(c.head_dim)));
+    aa.sms = h->att_sms ? h->att_sms : h->sms;
+    aa.split_mode = h->att_mode;
     // each output row stored into the rank that keeps it, at this rank's head columns
     for (int g = 0; g < G; ++g) aa.sp_out[g] = reinterpret_cast<bf16*>(b.peer_mem[g] + b.off_att);
     aa.sp_ld = W;
@@ -1199,6 +1212,9 @@ int exn_open(const exn_config* cfg, exn_handle** out) {
         CK(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking));
         CK(cudaMalloc(&h->d_status, sizeof(int)));
         CK(cudaMemset(h->d_status, 0, sizeof(int)));
+        // the kernels' shared-memory limits are attributes of this device's context
+        CK(static_cast<cudaError_t>(gemm_prepare()));
+        CK(static_cast<cudaError_t>(attention_prepare()));
         return EXN_OK;
       }()) ||
       (rc = alloc_weights(h))) {
@@ -1210,6 +1226,7 @@ int exn_open(const exn_config* cfg, exn_handle** out) {
   for (size_t i = 0; i < h->spec.size(); ++i) h->index[h->spec[i].name] = static_cast<int>(i);
   h->loaded.assign(h->spec.size(), 0);
   h->prof.on = std::getenv("EXN_PROFILE") != nullptr;
+  if (const char* e = std::getenv("EXN_ATT_SINGLE")) h->att_mode = std::atoi(e) == 1 ? 1 : (std::atoi(e) == 0 ? 0 : 2);
   *out = h;
   return EXN_OK;
 }
@@ -1681,8 +1698,18 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
   aa.width = heads * 128;
   aa.kv_rows = kv_rows;
   aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+  aa.sms = h->att_sms ? h->att_sms : h->sms;
+  aa.split_mode = h->att_mode;
   if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_EINVAL, "attention launch failed: %d", rc);
   return check_status(h);
+}
+
+int exn_test_attention_split(exn_handle* h, int mode, int sms) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_attention_split: null handle");
+  if (mode < 0 || mode > 2 || sms < 0) return fail(h, EXN_EINVAL, "exn_test_attention_split: mode %d, sms %d", mode, sms);
+  h->att_mode = mode;
+  h->att_sms = sms;
+  return EXN_OK;
 }
 
 int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, int n, int width, int n0, int p) {

@@ -573,14 +573,15 @@ void temb_launch(float* emb, double sigma, int freq, cudaStream_t st) {
   k_temb<<<1, 128, 0, st>>>(emb, 1000.0 * sigma, freq);
 }
 
-void gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out, int act,
-                 int piece, cudaStream_t st) {
+int gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out, int act,
+                int piece, cudaStream_t st) {
   // rows a warp owns: 4 (a group of rows sharing each x read) when that still leaves >= 2 blocks
   // per SM of a 148-SM part, else 1 (x is staged once a block)
   const int rows = blocks_for(out, GEMV_WARPS * 4) >= 2 * 148 ? 4 : 1;
   const unsigned grid = blocks_for(out, GEMV_WARPS * rows);
   const int epc = kind == W_Q8 ? 16 : 8;  // x is staged in whole chunks of 32 lanes x epc floats
   const size_t sm = static_cast<size_t>(m) * ((in + 32 * epc - 1) / (32 * epc)) * (32 * epc) * sizeof(float);
+  if (m < 1 || m > GEMV_MAXM || sm > 48 * 1024) return -1;  // x is staged whole in the default 48 KB
   if (kind == W_Q8 && rows == 4)
     k_gemv<W_Q8, 4><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
   else if (kind == W_Q8)
@@ -589,6 +590,7 @@ void gemv_launch(int kind, const void* w, const __half* wd, const float* x, floa
     k_gemv<W_BF16, 1><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
   else
     k_gemv<W_F32, 1><<<grid, GEMV_WARPS * 32, sm, st>>>(w, wd, x, y, m, in, out, act, piece, rows);
+  return static_cast<int>(cudaGetLastError());
 }
 
 void q8_raw_to_bf16_launch(const uint8_t* raw, bf16* dst, long long rows, int cols, long long row0, int ilv,

@@ -105,6 +105,10 @@ struct AttnArgs {
   int heads = 0, width = 0;
   int kv_rows = 0;           // row capacity of one sample's K/V
   float scale_log2 = 0.f;    // log2(e) / sqrt(128)
+  // work split: CTAs of two query tiles, except (split_mode 2) a last round that would fill at most
+  // half of the SMS multiprocessors runs as one-tile CTAs; split_mode 0: two-tile CTAs only, 1:
+  // one-tile CTAs only.  Each query row's arithmetic is the same in every mode.
+  int sms = 0, split_mode = 2;
   // sequence-parallel (sp_out[0] != null): query row qi of the pass is stored into the rank that
   // keeps it, at sp_out[owner] + local * sp_ld + sp_col0 + head * 128: prefix rows qi < sp_img0
   // (first pass) belong to rank qi / sp_pl at local qi % sp_pl; image row i = qi - sp_img0 to
@@ -113,6 +117,9 @@ struct AttnArgs {
   int sp_ld = 0, sp_col0 = 0, sp_pl = 0, sp_pl_loc = 0, sp_nl = 0, sp_img0 = 0;
 };
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st);
+// kernel attributes (dynamic shared memory) on the current device: 0 or a cudaError_t
+int attention_prepare();
+int gemm_prepare();
 
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.
@@ -133,9 +140,10 @@ void rope_table_launch(float2* table, int r0, int count, int p, int h, int w, in
 void temb_launch(float* emb, double sigma, int freq, cudaStream_t st);
 // Weight kinds for the small GEMVs
 enum WKind : int { W_Q8 = 0, W_BF16 = 1, W_F32 = 2 };
-// y[m][out] = act(x[m][in] . W[out][in]); act 0 none, 1 silu, 2 tanh on columns of pieces 1 and 3 (of 4)
-void gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out,
-                 int act, int piece, cudaStream_t st);
+// y[m][out] = act(x[m][in] . W[out][in]); act 0 none, 1 silu, 2 tanh on columns of pieces 1 and 3 (of 4).
+// 0, -1 (m > 2 or m x in floats beyond 48 KB of shared memory) or the launch's cudaError_t.
+int gemv_launch(int kind, const void* w, const __half* wd, const float* x, float* y, int m, int in, int out,
+                int act, int piece, cudaStream_t st);
 // GGUF Q8_0 blocks (34 B) -> bf16 rows, row r written at dst_row(r) (gate_up interleave when ilv > 0)
 void q8_raw_to_bf16_launch(const uint8_t* raw, bf16* dst, long long rows, int cols, long long row0, int ilv,
                            cudaStream_t st);

@@ -441,6 +441,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       griddep_wait();
       int stage = 0;
       uint32_t phase = 0;
+      int last_phase[C::STAGES];  // the last phase of each stage whose copies this CTA issued
+#pragma unroll
+      for (int s = 0; s < C::STAGES; ++s) last_phase[s] = -1;
       bool ok = true;
       for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
         int mb, nb;
@@ -456,13 +459,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * BK, mb * 256 + rank * 128);
           tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * BK, nb * C::BN + rank * 128);
+          last_phase[stage] = static_cast<int>(phase);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (!ok) __nanosleep(50000);  // copies already issued land before the CTA moves on
+      if (!ok && rank == 0) {
+        // the copies already issued land before the pair moves on: each stage's full barrier (the
+        // leader's) counts both CTAs' bytes of a phase, so waiting, bounded, for the last phase
+        // armed here covers the peer's copies of that phase too; the peer cannot leave before this
+        // wait ends (both CTAs meet at the cluster barrier at the end of the kernel)
+        volatile int no_abort = 0;
+        for (int s = 0; s < C::STAGES; ++s)
+          if (last_phase[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(last_phase[s]), &no_abort, nullptr, 0);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
@@ -576,12 +588,6 @@ int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* d
 template <int BN, int EPI>
 static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
   using C = GemmCfg<BN>;
-  static bool attr = false;  // per instantiation; set before the first launch
-  if (!attr) {
-    if (cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
   CUtensorMap ta, tb;
   const uint64_t da[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M)};
   const uint64_t sa[1] = {static_cast<uint64_t>(g.lda) * 2};
@@ -604,12 +610,6 @@ static int launch_bn(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t
 template <int EPI>
 static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
   using C = Gemm2Cfg;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(k_gemm2<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
   CUtensorMap ta, tb;
   const uint64_t da[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M)};
   const uint64_t sa[1] = {static_cast<uint64_t>(g.lda) * 2};
@@ -627,6 +627,30 @@ static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream
   group_m = group_m > num_m ? num_m : group_m;
   return static_cast<int>(launch_pdl(k_gemm2<EPI>, dim3(clusters * 2), dim3(GEMM_THREADS), C::SMEM, st, ta, tb,
                                      g.M, g.N, g.K, group_m, g.ep, d_status));
+}
+
+template <int BN, int EPI>
+static cudaError_t allow_smem_bn() {
+  return cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM);
+}
+template <int EPI>
+static cudaError_t allow_smem_pair() {
+  return cudaFuncSetAttribute(k_gemm2<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Cfg::SMEM);
+}
+
+// The dynamic shared-memory limit of every GEMM instantiation, raised on the CURRENT device (the
+// attribute belongs to one device's context, so each handle's device gets it at exn_open).
+int gemm_prepare() {
+  const cudaError_t e[] = {
+      allow_smem_pair<EPI_QKV>(),        allow_smem_pair<EPI_SWIGLU>(),   allow_smem_pair<EPI_GATE_RESID>(),
+      allow_smem_pair<EPI_F32>(),        allow_smem_pair<EPI_BF16>(),     allow_smem_pair<EPI_GELU_BF16>(),
+      allow_smem_bn<256, EPI_QKV>(),     allow_smem_bn<256, EPI_SWIGLU>(), allow_smem_bn<64, EPI_PROJ>(),
+      allow_smem_bn<256, EPI_GATE_RESID>(), allow_smem_bn<128, EPI_GATE_RESID>(), allow_smem_bn<256, EPI_F32>(),
+      allow_smem_bn<64, EPI_F32>(),      allow_smem_bn<256, EPI_BF16>(),  allow_smem_bn<64, EPI_BF16>(),
+      allow_smem_bn<256, EPI_GELU_BF16>()};
+  for (cudaError_t x : e)
+    if (x != cudaSuccess) return static_cast<int>(x);
+  return 0;
 }
 
 static bool use_pairs() {

@@ -96,6 +96,7 @@ def lib():
         # testing entry points (include/exn_b200_testing.h)
         "exn_test_gemm": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
+        "exn_test_attention_split": (ctypes.c_int, [H, ctypes.c_int, ctypes.c_int]),
         "exn_test_ln_mod": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_qkv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
         "exn_test_trace": (ctypes.c_int, [H, vp, ctypes.c_size_t]),

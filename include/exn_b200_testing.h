@@ -23,6 +23,12 @@ int exn_test_gemm(exn_handle* h, const void* a, const void* b, float* c, int m, 
 int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                        int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
 
+/* How the attention kernel splits its work, for this handle's later calls: MODE 2 (the default)
+ * runs CTAs of two 128-query tiles except that a last round filling at most half of SMS
+ * multiprocessors runs as one-tile CTAs; MODE 0 two-tile CTAs only; MODE 1 one-tile CTAs only.
+ * SMS 0 is the device's count.  Every mode gives each query row the same arithmetic. */
+int exn_test_attention_split(exn_handle* h, int mode, int sms);
+
 /* LayerNorm(x) * (1 + mod[row kind]) -> bf16 (x_ln_mod, src/cuda/dit.cu:17-32):
  * rows n, mod [2][width] (row 1 for prompt rows, n0 + t < p). */
 int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, int n, int width, int n0, int p);

@@ -54,6 +54,8 @@ CASES = {
 FULL = {
     # the full 32-block D=4096 DiT at 1024^2 (64 x 64 latent), 128 text rows, 8 steps
     "cfg2_euler": dict(shape=dict(), p=128, h=64, w=64, euler=True),
+    # 1536 x 1024 (a 64 x 96 latent, a non-square RoPE grid), 256 text rows, 8 steps
+    "cfg3_euler": dict(shape=dict(), p=256, h=64, w=96, euler=True),
 }
 
 
@@ -127,7 +129,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-dir", default=os.environ.get("EXN_REF_INSPECT"),
                     help="the reference tree's inspect/ directory (holds ref_dit.py); or set EXN_REF_INSPECT")
-    ap.add_argument("--full", action="store_true", help="also the full D=4096 8-step case (tens of minutes)")
+    ap.add_argument("--full", action="store_true", help="also the full D=4096 8-step cases (tens of minutes each)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     if not args.ref_dir:

@@ -173,8 +173,32 @@ def test_gguf_upload_equals_synthetic(tmp_path, tiny, tiny_sw, mtype):
     v0 = tiny.velocity(ctx[0], p, lat[0], h, w, 0.5)
     if mtype == "q8_0":
         assert O.rel_l2(v, v0) < 1e-6
-    else:   # the GEMV matrices keep f32 / bf16 / f16 values
+    elif mtype == "bf16":   # the GEMV matrices (timestep MLP, modulation) keep the bf16-rounded values
         assert O.rel_l2(v, v0) < 1e-2
+    else:   # f32 holds q * d exactly, f16 within 2^-11: only the GEMVs' sums and f16 roundings differ
+        assert O.rel_l2(v, v0) < 1e-3
+
+
+@pytest.mark.parametrize("mtype", ["f32", "bf16", "f16"])
+def test_gguf_gemm_matrix_conversion_is_exact(tmp_path, tiny_sw, mtype):
+    """A GEMM matrix stored as f32 / bf16 / f16 lands in the bf16 slab as the round-to-nearest bf16
+    of the stored value, bit for bit (f16 widens to f32 exactly first)."""
+    import torch
+    path = tmp_path / "dit.gguf"
+    write_gguf(path, tiny_sw, matrix_type=mtype)
+    name = "transformer_blocks.1.img_mlp.gate_up.weight"   # interleaved on the device: undone by the reader
+    qs, dq = tiny_sw.q8[name]
+    vals = O.q8_0_dequantize(qs, dq)
+    if mtype == "f16":
+        vals = vals.astype(np.float16).astype(np.float32)
+    want = torch.from_numpy(np.ascontiguousarray(vals)).to(torch.bfloat16).view(torch.int16).numpy()
+    d = E.upload_dit(path, **TINY)
+    try:
+        got = np.empty(want.shape, dtype=np.int16)
+        d._ck(E.lib().exn_test_weight_bf16(d.h, name.encode(), got.ctypes.data, got.size))
+    finally:
+        d.close()
+    assert np.array_equal(got, want)
 
 
 def test_errors_are_reported():

@@ -85,6 +85,35 @@ def test_attention_mask_cases(dit, case):
         assert err < 3e-3 + 2 ** -8, (b, err)
 
 
+@pytest.mark.parametrize("nq", [300, 700])
+def test_attention_work_splits_are_bit_identical(dit, nq):
+    """The attention kernel's work splits (two-tile CTAs only; one-tile CTAs only; two-tile CTAs with a
+    short last round run as one-tile CTAs, forced here by planning for fewer SMs) give every query row the
+    same bits, also for a row count that is not a multiple of 256."""
+    batch, q0, p, heads = 1, 0, 40, 4
+    l = nq
+    w = heads * 128
+    g = torch.Generator().manual_seed(nq)
+    q = ((torch.rand(batch, nq, w, generator=g) * 4 - 2)).to(torch.bfloat16).cuda()
+    k = ((torch.rand(batch, l, w, generator=g) * 4 - 2)).to(torch.bfloat16).cuda()
+    v = ((torch.rand(batch, l, w, generator=g) * 2 - 1)).to(torch.bfloat16).cuda()
+    items = -(-nq // 256) * heads * batch           # two-tile work items
+    plan = items - 2                                # a last round of 2 items: split into 4 one-tile CTAs
+    assert 0 < items % plan and 2 * (items % plan) <= plan
+    outs = []
+    try:
+        for mode, sms in [(0, 0), (1, 0), (2, plan)]:
+            dit._ck(E.lib().exn_test_attention_split(dit.h, mode, sms))
+            o = torch.full((batch, nq, w), float("nan"), dtype=torch.bfloat16, device="cuda")
+            dit._ck(E.lib().exn_test_attention(dit.h, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                               batch, nq, q0, p, l, 0, 0, heads, l))
+            outs.append(o.view(torch.int16).cpu())
+    finally:
+        dit._ck(E.lib().exn_test_attention_split(dit.h, 2, 0))
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], outs[2])
+
+
 def test_ln_mod_row_selection(dit):
     # metal-kernels-test.lisp:91-102: rows n0 + t < p take the second modulation row
     wd, n, n0, p = 4096, 9, 3, 6
