@@ -1725,7 +1725,9 @@ int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, in
 int exn_test_qkv(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p, int hh,
                  int ww, int kv_rows) {
   if (!h || !y || !q || !k || !v) return fail(h, EXN_EINVAL, "exn_test_qkv: null argument");
-  if (layer < 0 || layer >= h->cfg.layers || n0 + n > kv_rows) return fail(h, EXN_EINVAL, "exn_test_qkv: bad sizes");
+  if (layer < 0 || layer >= h->cfg.layers || n < 1 || n0 < 0 || p < 0 || hh < 1 || ww < 1 || n0 + n > kv_rows ||
+      n0 + n > p + hh * ww)  // the rows' RoPE comes from the table of the p + hh x ww sequence rows
+    return fail(h, EXN_EINVAL, "exn_test_qkv: bad sizes");
   int rc;
   if ((rc = use_device(h))) return rc;
   const int W = h->cfg.width, L = p + hh * ww;
