@@ -336,6 +336,15 @@ def run_exn(args):
         d.profile(False)
     finite = bool(np.isfinite(zs).all())
     barrier(dist)
+    # N > 1: BASELINE config 4 (one 8704-row edit shared by all N GPUs, Ulysses) after the replica timing
+    sp = None
+    if world > 1 and args.workload == "cfg2" and not args.no_sp_edit:
+        sp_ms, sp_e2e = edit_pictures(d, rank, world, dist, 3, 3)
+        sp = {"workload": "BASELINE config 4: edit, 4096 target + 4096 reference + 512 text rows (8704), 8 Euler "
+                          "steps, one picture over all %d GPUs (Ulysses sequence parallelism)" % world,
+              "ms_per_picture": round(sp_ms, 2), "images_per_s": round(1e3 / sp_ms, 4),
+              "e2e_ms_per_picture": round(sp_e2e, 2), "steps": 3, "warmup": 3, "scaling": "strong",
+              "timing": "CUDA events on the library's stream around each exn_generate's device part, max over ranks"}
     if rank != 0:
         d.close()
         return None
@@ -395,6 +404,9 @@ def run_exn(args):
         "gpu_launches": launches * args.steps * world,
         "gpu_launches_per_step": launches,
     }
+    if sp is not None:
+        sp["tc_peak_frac"] = round(sum(edit_flops(args.layers)) / (sp["ms_per_picture"] * 1e-3) / world / 1e12 / bt, 4)
+        out["sp_edit"] = sp
     if args.workload == "cfg5":
         out["config"]["workload"] = ("BASELINE config 5: %d pictures (seeds 0..%d, 1024^2, 128 text rows, 8 steps), "
                                      "batches of %d per GPU" % (args.pictures, args.pictures - 1, args.batch))
@@ -414,6 +426,37 @@ def run_exn(args):
     return out
 
 
+def edit_pictures(d, rank, world, dist, steps, warmup):
+    """BASELINE config 4 on handle D shared by all WORLD ranks (Ulysses when WORLD > 1): WARMUP then
+    STEPS edit pictures through exn_generate, each a new prompt key.  Device ms (CUDA events on the
+    library's stream, inputs in HBM) and wall ms a picture, both max over ranks."""
+    import exn_b200 as E
+    from oracle import dit_oracle as O
+    if world > 1:
+        obj = [E.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        d.comm_init(obj[0], rank, world)
+    p_text, a = 512, 8
+    ctx, lat = O.synth_inputs(O.Shape(), p_text, H, WW, seed=7)
+    _, ref = O.synth_inputs(O.Shape(), 1, H, WW, seed=8)
+    refarg = (a, ref[0], H, WW)
+    for i in range(warmup):
+        d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("warm", i), ref=refarg)
+    barrier(dist)
+    dev_ms = 0.0
+    t0 = time.perf_counter()
+    for i in range(steps):
+        d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("edit", i), ref=refarg)
+        dev_ms += d.last_call_ms()
+    dt = (time.perf_counter() - t0) / steps
+    ms = max_over_ranks(dist, dev_ms / steps)
+    e2e_ms = max_over_ranks(dist, dt * 1e3)
+    if world > 1:
+        d.comm_destroy()
+    barrier(dist)
+    return ms, e2e_ms
+
+
 def run_edit(args):
     """one edit picture (4096 target rows, a 4096-row reference picture and 512 text
     rows: 8704 rows) through all N GPUs at once (Ulysses sequence parallelism), 8 Euler steps; a new
@@ -427,29 +470,9 @@ def run_edit(args):
     torch.cuda.set_device(local)
     d = E.Dit(device=local, layers=args.layers)
     d.load_synthetic(1)
-    if world > 1:
-        obj = [E.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        d.comm_init(obj[0], rank, world)
-    p_text, a = 512, 8
-    ctx, lat = O.synth_inputs(O.Shape(), p_text, H, WW, seed=7)
-    _, ref = O.synth_inputs(O.Shape(), 1, H, WW, seed=8)
-    refarg = (a, ref[0], H, WW)
-    for i in range(args.warmup):
-        d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("warm", i), ref=refarg)
-    barrier(dist)
-    dev_ms = 0.0
     with Clocks(gpu_index(local)) as clk:
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            z = d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("edit", i), ref=refarg)
-            dev_ms += d.last_call_ms()
-        dt = (time.perf_counter() - t0) / args.steps
-    ms = max_over_ranks(dist, dev_ms / args.steps)
-    e2e_ms = max_over_ranks(dist, dt * 1e3)
+        ms, e2e_ms = edit_pictures(d, rank, world, dist, args.steps, args.warmup)
     launches = d.launch_count()
-    if world > 1:
-        d.comm_destroy()
     d.close()
     barrier(dist)
     if rank != 0:
@@ -526,6 +549,8 @@ def main():
                     help="cfg2: one picture per GPU per step (default); cfg4: one 8704-row edit over all GPUs; "
                          "cfg5: 64 pictures split over the GPUs")
     ap.add_argument("--pictures", type=int, default=64, help="cfg5: pictures in the job")
+    ap.add_argument("--no-sp-edit", action="store_true",
+                    help="N > 1: skip the config-4 edit shared by all GPUs that follows the replica timing")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

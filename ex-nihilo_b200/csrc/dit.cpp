@@ -175,6 +175,8 @@ struct exn_handle {
   // attention work split (AttnArgs::split_mode, EXN_ATT_SINGLE at open) and the SM count it plans
   // for (0: the device's); a testing entry point may change both
   int att_mode = 2, att_sms = 0;
+  // GEMM tiles: 1 256 x 256 on CTA pairs (EXN_GEMM_PAIRS=0 at open: 128-row tiles of one CTA)
+  int gemm_pairs = 1;
   cudaStream_t st = nullptr;
   std::string err;
   int* d_status = nullptr;
@@ -565,6 +567,7 @@ int gemm(exn_handle* h, const bf16* a, long long lda, const bf16* b, long long l
   g.K = K;
   g.epi = epi;
   g.ep = ep;
+  g.pairs = h->gemm_pairs;
   const int r = gemm_launch(g, h->d_status, h->sms, h->st);
   if (r) return fail(h, EXN_ECUDA, "GEMM %dx%dx%d (epilogue %d) launch failed: %d", M, N, K, epi, r);
   return EXN_OK;
@@ -1215,6 +1218,7 @@ int exn_open(const exn_config* cfg, exn_handle** out) {
         // the kernels' shared-memory limits are attributes of this device's context
         CK(static_cast<cudaError_t>(gemm_prepare()));
         CK(static_cast<cudaError_t>(attention_prepare()));
+        CK(static_cast<cudaError_t>(gemm_q8_prepare()));
         return EXN_OK;
       }()) ||
       (rc = alloc_weights(h))) {
@@ -1226,6 +1230,7 @@ int exn_open(const exn_config* cfg, exn_handle** out) {
   for (size_t i = 0; i < h->spec.size(); ++i) h->index[h->spec[i].name] = static_cast<int>(i);
   h->loaded.assign(h->spec.size(), 0);
   h->prof.on = std::getenv("EXN_PROFILE") != nullptr;
+  if (const char* e = std::getenv("EXN_GEMM_PAIRS")) h->gemm_pairs = std::atoi(e) != 0;
   if (const char* e = std::getenv("EXN_ATT_SINGLE")) h->att_mode = std::atoi(e) == 1 ? 1 : (std::atoi(e) == 0 ? 0 : 2);
   *out = h;
   return EXN_OK;
@@ -1704,6 +1709,12 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
   return check_status(h);
 }
 
+int exn_test_gemm_pairs(exn_handle* h, int pairs) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_gemm_pairs: null handle");
+  h->gemm_pairs = pairs != 0;
+  return EXN_OK;
+}
+
 int exn_test_attention_split(exn_handle* h, int mode, int sms) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_attention_split: null handle");
   if (mode < 0 || mode > 2 || sms < 0) return fail(h, EXN_EINVAL, "exn_test_attention_split: mode %d, sms %d", mode, sms);
@@ -1808,6 +1819,118 @@ int exn_test_synth_normal(exn_handle* h, float* d, int64_t n, uint64_t seed, uin
   synth_f32_launch(d, n, seed, stream, static_cast<float>(std_dev / ih_std), 0.f, h->st);
   CK(cudaGetLastError());
   return check_status(h);
+}
+
+int exn_test_synth_q8(exn_handle* h, void* d_qs, void* d_d, int64_t n, uint64_t seed, uint32_t stream,
+                      double std_dev) {
+  if (!h || !d_qs || !d_d || n <= 0 || n % 32) return fail(h, EXN_EINVAL, "exn_test_synth_q8: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  const double ih_std = std::sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0);
+  synth_q8_launch(static_cast<int8_t*>(d_qs), static_cast<__half*>(d_d), n, seed, stream,
+                  static_cast<float>(std_dev / ih_std), h->st);
+  CK(cudaGetLastError());
+  return check_status(h);
+}
+
+int exn_test_gemm_q8(exn_handle* h, const void* a, const void* qs, const void* d, float* c, int m, int n, int k,
+                     int reps, double* ms) {
+  if (!h || !a || !qs || !d || !c || reps < 0) return fail(h, EXN_EINVAL, "exn_test_gemm_q8: bad argument");
+  if (n % 256 || k % 64) return fail(h, EXN_EINVAL, "exn_test_gemm_q8: n %d (multiple of 256), k %d (of 64)", n, k);
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  __half* dk = nullptr;
+  CK(cudaMalloc(&dk, static_cast<size_t>(n) * (k / 32) * 2));
+  GemmArgs g;
+  g.a = static_cast<const bf16*>(a);
+  g.lda = k;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.epi = EPI_F32;
+  g.ep.out = c;
+  g.ep.ld_out = n;
+  int r = q8_scales_by_kblock_launch(static_cast<const __half*>(d), dk, n, k, h->st);
+  if (!r) r = gemm_q8_launch(g, static_cast<const int8_t*>(qs), dk, h->d_status, h->sms, h->st);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  if (!r && reps > 0) {
+    cudaEventCreate(&ev[0]);
+    cudaEventCreate(&ev[1]);
+    cudaEventRecord(ev[0], h->st);
+    for (int i = 0; i < reps && !r; ++i) r = gemm_q8_launch(g, static_cast<const int8_t*>(qs), dk, h->d_status, h->sms, h->st);
+    cudaEventRecord(ev[1], h->st);
+  }
+  if (r) {
+    cudaStreamSynchronize(h->st);
+    cudaFree(dk);
+    return fail(h, EXN_ECUDA, "Q8_0 GEMM %dx%dx%d launch failed: %d", m, n, k, r);
+  }
+  rc = check_status(h);
+  if (!rc && reps > 0 && ms) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ev[0], ev[1]);
+    *ms = t / reps;
+  }
+  for (cudaEvent_t e : ev)
+    if (e) cudaEventDestroy(e);
+  cudaFree(dk);
+  return rc;
+}
+
+int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k, int reps,
+                        double* ms) {
+  if (!h || !a || !b || !c || reps < 1 || !ms) return fail(h, EXN_EINVAL, "exn_test_gemm_timed: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  GemmEpi e;
+  e.out = c;
+  e.ld_out = n;
+  cudaEvent_t ev[2];
+  CK(cudaEventCreate(&ev[0]));
+  CK(cudaEventCreate(&ev[1]));
+  CK(cudaEventRecord(ev[0], h->st));
+  for (int i = 0; i < reps && !rc; ++i)
+    rc = gemm(h, static_cast<const bf16*>(a), k, static_cast<const bf16*>(b), k, m, n, k, EPI_F32, e);
+  CK(cudaEventRecord(ev[1], h->st));
+  if (!rc) rc = check_status(h);
+  if (!rc) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ev[0], ev[1]);
+    *ms = t / reps;
+  }
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  return rc;
+}
+
+int exn_test_weights_digest(exn_handle* h, uint64_t* out) {
+  if (!h || !out) return fail(h, EXN_EINVAL, "exn_test_weights_digest: null argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  unsigned long long* acc = nullptr;
+  CK(cudaMalloc(&acc, sizeof(unsigned long long)));
+  cudaMemsetAsync(acc, 0, sizeof(unsigned long long), h->st);
+  digest_launch(h->slab, h->slab_bytes & ~size_t(7), acc, h->st);
+  const exn_config& c = h->cfg;
+  const size_t W = c.width;
+  const struct {
+    const GemvW* g;
+    size_t n;
+  } gv[4] = {{&h->lin1, W * c.freq}, {&h->lin2, W * W}, {&h->mod, 4 * W * W}, {&h->nout, W * W}};
+  for (const auto& x : gv) {
+    if (!x.g->w) continue;
+    const size_t wb = x.g->kind == W_Q8 ? x.n : (x.g->kind == W_BF16 ? 2 * x.n : 4 * x.n);
+    digest_launch(x.g->w, wb & ~size_t(7), acc, h->st);
+    if (x.g->kind == W_Q8) digest_launch(x.g->d, (x.n / 32 * 2) & ~size_t(7), acc, h->st);
+  }
+  unsigned long long v = 0;
+  rc = cudaGetLastError() == cudaSuccess ? EXN_OK : fail(h, EXN_ECUDA, "exn_test_weights_digest: launch failed");
+  if (!rc && cudaMemcpyAsync(&v, acc, sizeof v, cudaMemcpyDeviceToHost, h->st) != cudaSuccess)
+    rc = fail(h, EXN_ECUDA, "exn_test_weights_digest: copy failed");
+  if (!rc) rc = check_status(h);
+  cudaFree(acc);
+  *out = v;
+  return rc;
 }
 
 int exn_test_profile(exn_handle* h, int on) {

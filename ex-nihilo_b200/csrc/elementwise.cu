@@ -540,6 +540,21 @@ __global__ void k_synth_f32(float* __restrict__ v, long long n, uint64_t seed, u
   if (i < n) v[i] = __fadd_rn(base, __fmul_rn(static_cast<float>(synth_offset(seed, stream, i)), scale));
 }
 
+// An order-independent digest of N 8-byte words: the sum of a mix of each word with its index.
+__global__ void k_digest(const uint64_t* __restrict__ p, long long n, unsigned long long* out) {
+  unsigned long long acc = 0;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    uint64_t z = p[i] ^ (static_cast<uint64_t>(i) * 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    acc += z ^ (z >> 31);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(out, acc);
+}
+
 inline unsigned blocks_for(long long n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
 }  // namespace
@@ -625,6 +640,13 @@ void f16_to_f32_launch(const __half* src, float* dst, long long n, cudaStream_t 
 
 void bf16_to_f32_launch(const bf16* src, float* dst, long long n, cudaStream_t st) {
   k_bf16_to_f32<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, n);
+}
+
+void digest_launch(const void* p, size_t bytes, unsigned long long* out, cudaStream_t st) {
+  const long long n = static_cast<long long>(bytes / 8);
+  if (n <= 0) return;
+  k_digest<<<static_cast<unsigned>(n < 148LL * 2048 ? blocks_for(n, 256) : 148 * 8), 256, 0, st>>>(
+      static_cast<const uint64_t*>(p), n, out);
 }
 
 void wait_probe_launch(int* status, unsigned long long limit_ns, cudaStream_t st) {

@@ -91,6 +91,8 @@ struct GemmArgs {
   int M = 0, N = 0, K = 0;
   int epi = EPI_F32;
   GemmEpi ep;
+  // tile shape: 1 (default) 256 x 256 tiles on CTA pairs where N allows, 0 128-row tiles of one CTA
+  int pairs = 1;
 };
 
 // C = A B^T through the tcgen05 kernel.  0, or a cudaError_t / -1 (bad shape).
@@ -120,6 +122,14 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st);
 // kernel attributes (dynamic shared memory) on the current device: 0 or a cudaError_t
 int attention_prepare();
 int gemm_prepare();
+int gemm_q8_prepare();
+
+// C = A . (q d)^T with the weights as Q8_0 (gemm_q8.cu): QS int8 [N][K], DK the fp16 scales laid out
+// by k-block ([K/64][N][2], q8_scales_by_kblock_launch from GGUF's [N][K/32]).  Epilogues EPI_F32
+// and EPI_SWIGLU.  0, -1 (bad shape), -4 (tensor map) or a cudaError_t.
+int gemm_q8_launch(const GemmArgs& g, const int8_t* qs, const __half* dk, int* d_status, int num_sms,
+                   cudaStream_t st);
+int q8_scales_by_kblock_launch(const __half* d, __half* out, int n, int k, cudaStream_t st);
 
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.
@@ -166,6 +176,8 @@ void synth_f32_launch(float* v, long long n, uint64_t seed, uint32_t stream, flo
 void q8_to_bf16_launch(const int8_t* qs, const __half* d, bf16* dst, long long rows, int cols, long long row0,
                        int ilv, cudaStream_t st);
 void add_scalar_launch(float* v, long long n, float a, cudaStream_t st);
+// *out += an order-independent digest of BYTES (a multiple of 8) at P
+void digest_launch(const void* p, size_t bytes, unsigned long long* out, cudaStream_t st);
 // one CTA whose bounded wait on an mbarrier nothing arrives on runs out after LIMIT_NS
 void wait_probe_launch(int* status, unsigned long long limit_ns, cudaStream_t st);
 

@@ -95,7 +95,12 @@ def lib():
         "exn_comm_destroy": (ctypes.c_int, [H]),
         # testing entry points (include/exn_b200_testing.h)
         "exn_test_gemm": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "exn_test_gemm_q8": (ctypes.c_int, [H, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_double)]),
+        "exn_test_gemm_timed": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               ctypes.POINTER(ctypes.c_double)]),
         "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
+        "exn_test_gemm_pairs": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_attention_split": (ctypes.c_int, [H, ctypes.c_int, ctypes.c_int]),
         "exn_test_ln_mod": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_qkv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
@@ -103,6 +108,9 @@ def lib():
         "exn_test_weight_bf16": (ctypes.c_int, [H, ctypes.c_char_p, vp, ctypes.c_size_t]),
         "exn_test_synth_normal": (ctypes.c_int, [H, vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
                                                  ctypes.c_double]),
+        "exn_test_synth_q8": (ctypes.c_int, [H, vp, vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,
+                                             ctypes.c_double]),
+        "exn_test_weights_digest": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_uint64)]),
         "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 4),
         "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_launch_count": (ctypes.c_longlong, [H]),

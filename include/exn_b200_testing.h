@@ -18,10 +18,26 @@ extern "C" {
  * the tcgen05 GEMM; all device pointers. */
 int exn_test_gemm(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k);
 
+/* The same product with B as Q8_0 weights, converted to bf16 inside the GEMM (gemm_q8.cu): QS
+ * int8 [n][k], D fp16 scales [n][k/32] (GGUF's order), device pointers; n a multiple of 256.  The
+ * reference keeps its weights this way on the device (src/cuda-dit.lisp:71-76).  With REPS > 0
+ * the GEMM then runs REPS more times back to back and *MS receives the mean time of one (CUDA
+ * events on the handle's stream). */
+int exn_test_gemm_q8(exn_handle* h, const void* a, const void* qs, const void* d, float* c, int m, int n, int k,
+                     int reps, double* ms);
+
+/* exn_test_gemm run REPS times back to back; *MS the mean time of one (CUDA events). */
+int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k, int reps,
+                        double* ms);
+
 /* Masked attention (xa_lim, src/cuda/dit.cu:60-66) on bf16 device tensors:
  * q [batch][nq][heads*128], k/v [batch][kv_rows][heads*128], out like q. */
 int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                        int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
+
+/* The GEMM tiles of this handle's later calls: PAIRS 1 (the default) 256 x 256 tiles on CTA pairs
+ * wherever N is a multiple of 256, 0 128-row tiles of one CTA everywhere. */
+int exn_test_gemm_pairs(exn_handle* h, int pairs);
 
 /* How the attention kernel splits its work, for this handle's later calls: MODE 2 (the default)
  * runs CTAs of two 128-query tiles except that a last round filling at most half of SMS
@@ -51,6 +67,18 @@ int exn_test_weight_bf16(exn_handle* h, const char* name, void* host_bf16, size_
 /* N floats offset * scale from the synthetic generator (stream, seed) into
  * device memory: the oracle's synth_normal. */
 int exn_test_synth_normal(exn_handle* h, float* d, int64_t n, uint64_t seed, uint32_t stream, double std);
+
+/* N values of the synthetic generator (stream, seed, N(0, std) before quantisation) as Q8_0, the
+ * way exn_load_synthetic makes each matrix: int8 D_QS [n] and fp16 D_D [n / 32], device pointers.
+ * The same bits as the test oracle's SynthWeights, made in milliseconds instead of minutes for the
+ * full-size checks. */
+int exn_test_synth_q8(exn_handle* h, void* d_qs, void* d_d, int64_t n, uint64_t seed, uint32_t stream,
+                      double std_dev);
+
+/* An order-independent 64-bit digest of every weight the handle holds on the device (the bf16 slab
+ * with the norm vectors, and the GEMV matrices in their stored form): two handles loaded with the
+ * same weights the same way have the same digest. */
+int exn_test_weights_digest(exn_handle* h, uint64_t* out);
 
 /* Turn per-category kernel timing on or off (also on when EXN_PROFILE is set
  * at open): CUDA events recorded on the handle's stream between the GEMM,

@@ -50,3 +50,30 @@ def write_gguf(path, sw: "O.SynthWeights", arch="qwen_image", drop=(), extra=(),
     wr.write_kv_data_to_file()
     wr.write_tensors_to_file()
     wr.close()
+
+
+def write_gguf_streaming(path, shape: "O.Shape", tensor, arch="qwen_image"):
+    """A full-size synthetic GGUF written tensor by tensor, so only one tensor is in host memory at a
+    time.  TENSOR(name, dims) gives a 1-D tensor as fp32, or a matrix as Q8_0 (qs int8 (rows, cols),
+    d fp16 (rows, cols / 32))."""
+    import gguf
+    wr = gguf.GGUFWriter(str(path), arch=arch)
+    specs = O.expected_tensors(shape)
+    for name, dims in specs:
+        if len(dims) == 1:
+            wr.add_tensor_info(O.PREFIX + name, (dims[0],), np.dtype(np.float32), dims[0] * 4)
+        else:
+            cols, rows = dims
+            wr.add_tensor_info(O.PREFIX + name, (rows, cols // 32 * 34), np.dtype(np.uint8), rows * cols // 32 * 34,
+                               raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+    wr.write_header_to_file()
+    wr.write_kv_data_to_file()
+    wr.write_ti_data_to_file()
+    for name, dims in specs:
+        t = tensor(name, dims)
+        if len(dims) == 1:
+            wr.write_tensor_data(np.ascontiguousarray(t, dtype=np.float32))
+        else:
+            qs, d = t
+            wr.write_tensor_data(O.q8_0_pack(qs, d).reshape(dims[1], dims[0] // 32 * 34))
+    wr.close()

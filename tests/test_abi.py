@@ -114,3 +114,16 @@ def test_prefix_keys():
     assert E.prefix_key_of(None) == 0
     assert E.prefix_key_of("a prompt") == E.prefix_key_of("a prompt") != 0
     assert E.prefix_key_of(("edit", 1)) != E.prefix_key_of(("edit", 2))
+
+
+def test_streaming_gguf_writer_equals_the_whole_file_writer(tmp_path):
+    """The full-size upload test writes its 7.6 GB GGUF tensor by tensor; at a small shape that writer
+    produces the same bytes as the writer the other tests use, and passes open-dit's checks."""
+    from oracle.synth_gguf import write_gguf_streaming
+    sh = O.Shape(**TINY)
+    sw = O.SynthWeights.make(sh, seed=1)
+    a, b = tmp_path / "a.gguf", tmp_path / "b.gguf"
+    write_gguf(a, sw)
+    write_gguf_streaming(b, sh, lambda name, dims: sw.vec[name] if len(dims) == 1 else sw.q8[name])
+    assert a.read_bytes() == b.read_bytes()
+    E.check_gguf(b, **TINY)

@@ -173,10 +173,10 @@ def test_gguf_upload_equals_synthetic(tmp_path, tiny, tiny_sw, mtype):
     v0 = tiny.velocity(ctx[0], p, lat[0], h, w, 0.5)
     if mtype == "q8_0":
         assert O.rel_l2(v, v0) < 1e-6
-    elif mtype == "bf16":   # the GEMV matrices (timestep MLP, modulation) keep the bf16-rounded values
+    elif mtype == "f32":   # f32 holds q * d exactly: only the GEMVs' order of summation differs
+        assert O.rel_l2(v, v0) < 5e-3
+    else:   # the GEMV matrices (timestep MLP, modulation) keep the f16- or bf16-rounded values
         assert O.rel_l2(v, v0) < 1e-2
-    else:   # f32 holds q * d exactly, f16 within 2^-11: only the GEMVs' sums and f16 roundings differ
-        assert O.rel_l2(v, v0) < 1e-3
 
 
 @pytest.mark.parametrize("mtype", ["f32", "bf16", "f16"])

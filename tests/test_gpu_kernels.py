@@ -39,6 +39,53 @@ def test_gemm_matches_fp64(dit, m, n, k):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("epi_shape", [(300, 512, 4096), (1088, 4096, 4096), (513, 12288, 4096)])
+def test_gemm_tile_shapes_are_bit_identical(dit, epi_shape):
+    """256 x 256 tiles on CTA pairs and 128-row tiles of one CTA give every output element the same
+    bits (the same k-order of the same MMAs), so a rank may pick either without changing a row."""
+    m, n, k = epi_shape
+    g = torch.Generator().manual_seed(m + n)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    b = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    outs = []
+    try:
+        for pairs in (1, 0):
+            dit._ck(E.lib().exn_test_gemm_pairs(dit.h, pairs))
+            c = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+            dit._ck(E.lib().exn_test_gemm(dit.h, a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k))
+            outs.append(c)
+    finally:
+        dit._ck(E.lib().exn_test_gemm_pairs(dit.h, 1))
+    assert torch.isfinite(outs[0]).all()
+    assert torch.equal(outs[0], outs[1])
+
+
+def q8_weights(n, k, seed):
+    """Random Q8_0 weights: int8 q in [-127, 127] and fp16 block scales, with their bf16 slab."""
+    g = torch.Generator().manual_seed(seed)
+    qs = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int32).to(torch.int8)
+    d = (torch.rand(n, k // 32, generator=g) * 0.002 + 1e-4).to(torch.float16)
+    w = (qs.float() * d.float().repeat_interleave(32, dim=1)).to(torch.bfloat16)
+    return qs, d, w
+
+
+@pytest.mark.parametrize("m,n,k", [(100, 256, 256), (300, 512, 192), (1000, 768, 1024), (4224, 1024, 4096)])
+def test_gemm_q8_equals_the_bf16_slab(dit, m, n, k):
+    """The GEMM that converts Q8_0 weights in shared memory gives the same bits as the GEMM on the
+    load-time bf16 slab of the same weights (each value round-to-nearest bf16 of q * d)."""
+    qs, d, w = q8_weights(n, k, m + n)
+    g = torch.Generator().manual_seed(k)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    c0 = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    c1 = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    dit._ck(E.lib().exn_test_gemm(dit.h, a.data_ptr(), w.cuda().data_ptr(), c0.data_ptr(), m, n, k))
+    qd, dd = qs.cuda(), d.cuda()
+    dit._ck(E.lib().exn_test_gemm_q8(dit.h, a.data_ptr(), qd.data_ptr(), dd.data_ptr(), c1.data_ptr(), m, n, k, 0,
+                                     None))
+    assert torch.isfinite(c1).all()
+    assert torch.equal(c0, c1)
+
+
 def attention_ref(q, k, v, q0, p, l, b0, b1, heads):
     """fp64 masked softmax attention on the (already bf16-rounded) inputs."""
     qq = q.double().reshape(q.shape[0], heads, 128)
