@@ -1761,6 +1761,42 @@ int exn_test_qkv(exn_handle* h, int layer, const void* y, void* q, void* k, void
   return check_status(h);
 }
 
+int exn_qkv_noalloc(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p, int hh,
+                    int ww, int kv_rows) {
+  if (!h || !y || !q || !k || !v) return fail(h, EXN_EINVAL, "exn_qkv_noalloc: null argument");
+  if (layer < 0 || layer >= h->cfg.layers || n < 1 || n0 < 0 || p < 0 || hh < 1 || ww < 1 || n0 + n > kv_rows ||
+      n0 + n > p + hh * ww)
+    return fail(h, EXN_EINVAL, "exn_qkv_noalloc: bad sizes");
+  const int W = h->cfg.width, L = p + hh * ww;
+  if (L > kNoAllocMaxRows)
+    return fail(h, EXN_EINVAL,
+                "exn_qkv_noalloc: a sequence of %d rows (p %d + %d x %d); its fixed RoPE scratch holds at most %d",
+                L, p, hh, ww, kNoAllocMaxRows);
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  float2* rope = nullptr;
+  if ((rc = noalloc_rope_scratch(h->cfg.device, &rope)))
+    return fail(h, EXN_ECUDA, "exn_qkv_noalloc: address of the RoPE scratch on device %d: %s", h->cfg.device,
+                rc > 0 ? cudaGetErrorString(static_cast<cudaError_t>(rc)) : "bad device");
+  // every row the GEMM reads (0 .. L-1) is written here first, so the previous call's table needs no clearing
+  rope_table_launch(rope, 0, L, p, hh, ww, 0, 0, 0, h->st);
+  GemmEpi eq;
+  eq.seg_in = n;
+  eq.n0 = n0;
+  eq.width = W;
+  eq.norm_q = h->norm_q + layer * 128;
+  eq.norm_k = h->norm_k + layer * 128;
+  eq.rope = rope;
+  eq.q = static_cast<bf16*>(q);
+  eq.k = static_cast<bf16*>(k);
+  eq.v = static_cast<bf16*>(v);
+  eq.kv_sample_stride = static_cast<long long>(kv_rows) * W;
+  if ((rc = gemm(h, static_cast<const bf16*>(y), W, h->w_qkv + static_cast<size_t>(layer) * 3 * W * W, W, n, 3 * W, W,
+                 EPI_QKV, eq)))
+    return rc;
+  return check_status(h);
+}
+
 int exn_test_trace(exn_handle* h, float* host, size_t floats) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_trace: null handle");
   h->trace_host = host;

@@ -131,6 +131,12 @@ int gemm_q8_launch(const GemmArgs& g, const int8_t* qs, const __half* dk, int* d
                    cudaStream_t st);
 int q8_scales_by_kblock_launch(const __half* d, __half* out, int n, int k, cudaStream_t st);
 
+// Scratch that needs no allocation (noalloc.cu): a RoPE table of at most kNoAllocMaxRows sequence
+// rows in a fixed device array.  Its address on DEVICE, which must be the current device: looked up
+// on the first call for that device, then cached.  0, -1 (bad argument) or a cudaError_t.
+constexpr int kNoAllocMaxRows = 8704;
+int noalloc_rope_scratch(int device, float2** table);
+
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.
 // single: one modulation row for every row (norm_out's scale).

@@ -104,6 +104,7 @@ def lib():
         "exn_test_attention_split": (ctypes.c_int, [H, ctypes.c_int, ctypes.c_int]),
         "exn_test_ln_mod": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_qkv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
+        "exn_qkv_noalloc": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
         "exn_test_trace": (ctypes.c_int, [H, vp, ctypes.c_size_t]),
         "exn_test_weight_bf16": (ctypes.c_int, [H, ctypes.c_char_p, vp, ctypes.c_size_t]),
         "exn_test_synth_normal": (ctypes.c_int, [H, vp, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32,

@@ -55,6 +55,20 @@ int exn_test_ln_mod(exn_handle* h, const float* x, void* y, const float* mod, in
 int exn_test_qkv(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p, int hh,
                  int ww, int kv_rows);
 
+/* exn_test_qkv without any device allocation, for callers that cannot call cudaMalloc: for
+ * instance a host that runs the DiT on a GPU lent to it by another server (ex-nihilo's tenant
+ * mode borrows its GPUs from illatio's chat server), whose memory that server's allocator already
+ * accounts for, so a new cudaMalloc would fail or take memory the owner counts on.  No counterpart
+ * in the reference.  The caller passes y, q, k and v as for exn_test_qkv; the RoPE table the
+ * GEMM's epilogue reads goes into a fixed 4.25 MiB device array of this library (every GPU that
+ * loads the library holds it until the process exits) instead of step buffers grown with
+ * cudaMalloc, so the sequence, p + hh x ww rows, may have at most 8704 rows (EXN_EINVAL beyond).
+ * The first call on a device looks up that array's address there; make that first call before any
+ * stream capture.  All calls on a device share the array: calls that overlap on the GPU (two
+ * handles of one device on different streams) race.  Each call rewrites every table row it reads. */
+int exn_qkv_noalloc(exn_handle* h, int layer, const void* y, void* q, void* k, void* v, int n, int n0, int p,
+                    int hh, int ww, int kv_rows);
+
 /* The residual stream x after every block (and txt_in's output first) of
  * the next exn_velocity call, copied into HOST (layers + 1 blocks of
  * rows x width floats, rows = the rows that call computes).  NULL disables. */
