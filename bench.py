@@ -344,7 +344,8 @@ def run_exn(args):
                           "steps, one picture over all %d GPUs (Ulysses sequence parallelism)" % world,
               "ms_per_picture": round(sp_ms, 2), "images_per_s": round(1e3 / sp_ms, 4),
               "e2e_ms_per_picture": round(sp_e2e, 2), "steps": 3, "warmup": 3, "scaling": "strong",
-              "timing": "CUDA events on the library's stream around each exn_generate's device part, max over ranks"}
+              "timing": "CUDA events on the library's stream around each exn_generate's device part, max over ranks",
+              "rank0_host_waits": getattr(edit_pictures, "host_waits", None)}
     if rank != 0:
         d.close()
         return None
@@ -444,11 +445,16 @@ def edit_pictures(d, rank, world, dist, steps, warmup):
         d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("warm", i), ref=refarg)
     barrier(dist)
     dev_ms = 0.0
+    s0 = d.comm_stats()
     t0 = time.perf_counter()
     for i in range(steps):
         d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("edit", i), ref=refarg)
         dev_ms += d.last_call_ms()
     dt = (time.perf_counter() - t0) / steps
+    s1 = d.comm_stats()
+    edit_pictures.host_waits = {"nccl_waits_per_picture": (s1[0] - s0[0]) / steps,
+                                "sleeps_per_picture": (s1[1] - s0[1]) / steps,
+                                "wait_ms_per_picture": round((s1[2] - s0[2]) * 1e3 / steps, 3)}
     ms = max_over_ranks(dist, dev_ms / steps)
     e2e_ms = max_over_ranks(dist, dt * 1e3)
     if world > 1:

@@ -228,6 +228,9 @@ struct exn_handle {
   int rank = 0, world = 1;
   double comm_timeout_s = 60.0;
   SpBufs sp;
+  // host cost of waiting for the communicator: calls of nccl_settle, their 50 us sleeps, seconds
+  long long settles = 0, settle_sleeps = 0;
+  double settle_s = 0.0;
 };
 
 namespace {
@@ -758,11 +761,16 @@ int nccl_fail(exn_handle* h, ncclResult_t r, const char* what) {
 // a non-blocking communicator's queued work, or its init, settled (bounded by comm_timeout_s)
 int nccl_settle(exn_handle* h, ncclComm_t comm, const char* what) {
   const auto t0 = std::chrono::steady_clock::now();
+  ++h->settles;
   while (true) {
     ncclResult_t st = ncclSuccess;
     ncclResult_t r = nccl().CommGetAsyncError(comm, &st);
     if (r != ncclSuccess) return nccl_fail(h, r, what);
-    if (st == ncclSuccess) return EXN_OK;
+    if (st == ncclSuccess) {
+      h->settle_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      return EXN_OK;
+    }
+    ++h->settle_sleeps;
     if (st != ncclInProgress) return nccl_fail(h, st, what);
     if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > h->comm_timeout_s) {
       nccl().CommAbort(comm);
@@ -1709,6 +1717,14 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
   return check_status(h);
 }
 
+int exn_test_comm_stats(exn_handle* h, long long* settles, long long* sleeps, double* seconds) {
+  if (!h) return fail(h, EXN_EINVAL, "exn_test_comm_stats: null handle");
+  if (settles) *settles = h->settles;
+  if (sleeps) *sleeps = h->settle_sleeps;
+  if (seconds) *seconds = h->settle_s;
+  return EXN_OK;
+}
+
 int exn_test_gemm_pairs(exn_handle* h, int pairs) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_gemm_pairs: null handle");
   h->gemm_pairs = pairs != 0;
@@ -1910,6 +1926,48 @@ int exn_test_gemm_q8(exn_handle* h, const void* a, const void* qs, const void* d
   for (cudaEvent_t e : ev)
     if (e) cudaEventDestroy(e);
   cudaFree(dk);
+  return rc;
+}
+
+int exn_test_gemm_i8(exn_handle* h, const void* a, const void* b, const float* sa, const float* sb, float* c, int m,
+                     int n, int k, int reps, double* ms) {
+  if (!h || !a || !b || !sa || !sb || !c || reps < 0) return fail(h, EXN_EINVAL, "exn_test_gemm_i8: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  GemmArgs g;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.epi = EPI_I8_F32;
+  g.ep.out = c;
+  g.ep.ld_out = n;
+  g.ep.mod = sa;
+  g.ep.norm_q = sb;
+  const int8_t* a8 = static_cast<const int8_t*>(a);
+  const int8_t* b8 = static_cast<const int8_t*>(b);
+  int r = gemm_i8_launch(g, a8, b8, h->d_status, h->sms, h->st);
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  if (!r && reps > 0) {
+    cudaEventCreate(&ev[0]);
+    cudaEventCreate(&ev[1]);
+    cudaEventRecord(ev[0], h->st);
+    for (int i = 0; i < reps && !r; ++i) r = gemm_i8_launch(g, a8, b8, h->d_status, h->sms, h->st);
+    cudaEventRecord(ev[1], h->st);
+  }
+  if (r) {
+    cudaStreamSynchronize(h->st);
+    for (cudaEvent_t e : ev)
+      if (e) cudaEventDestroy(e);
+    return fail(h, r == -1 ? EXN_EINVAL : EXN_ECUDA, "int8 GEMM %dx%dx%d launch failed: %d", m, n, k, r);
+  }
+  rc = check_status(h);
+  if (!rc && reps > 0 && ms) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ev[0], ev[1]);
+    *ms = t / reps;
+  }
+  for (cudaEvent_t e : ev)
+    if (e) cudaEventDestroy(e);
   return rc;
 }
 

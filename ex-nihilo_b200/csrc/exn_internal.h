@@ -21,6 +21,7 @@ enum EpiKind : int {
   EPI_GATE_RESID = 4,  // x[row] += tanh(gate)[mod row] * acc, f32           (to_out.0, img_mlp.out)
   EPI_SWIGLU = 5,      // out bf16 = silu(gate) * up, gate/up interleaved by 128 columns (img_mlp.gate_up)
   EPI_PROJ = 6,        // v channel-major and/or z += dsigma * v              (proj_out)
+  EPI_I8_F32 = 7,      // int8 product: f32 out = acc * mod[row] * norm_q[col] (a measured experiment)
 };
 
 // ranks of a sequence-parallel group that kernels address directly (peer pointers)
@@ -127,6 +128,8 @@ int gemm_q8_prepare();
 // C = A . (q d)^T with the weights as Q8_0 (gemm_q8.cu): QS int8 [N][K], DK the fp16 scales laid out
 // by k-block ([K/64][N][2], q8_scales_by_kblock_launch from GGUF's [N][K/32]).  Epilogues EPI_F32
 // and EPI_SWIGLU.  0, -1 (bad shape), -4 (tensor map) or a cudaError_t.
+// C = (A . B^T) * sa[row] * sb[col], A and B int8 (kind::i8), sa = g.ep.mod, sb = g.ep.norm_q, out f32
+int gemm_i8_launch(const GemmArgs& g, const int8_t* a, const int8_t* b, int* d_status, int num_sms, cudaStream_t st);
 int gemm_q8_launch(const GemmArgs& g, const int8_t* qs, const __half* dk, int* d_status, int num_sms,
                    cudaStream_t st);
 int q8_scales_by_kblock_launch(const __half* d, __half* out, int n, int k, cudaStream_t st);

@@ -195,11 +195,14 @@ struct Gemm2Cfg {
   static constexpr uint32_t IDESC = idesc_bf16(256, 256);
 };
 
-template <int EPI>
+// I8: A and B int8 (tcgen05.mma kind::i8, s32 accumulators): the same 128-byte k-blocks hold 128
+// elements, so the tile geometry, swizzle and descriptors are the bf16 ones; K counts elements.
+template <int EPI, bool I8 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     k_gemm2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
             int group_m, const GemmEpi ep, int* status) {
   using C = Gemm2Cfg;
+  constexpr int KB = I8 ? 2 * BK : BK;  // elements of a 128-byte k-block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -216,7 +219,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const int num_m = (M + 255) / 256, num_n = N / C::BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = K / BK;
+  const int num_kb = K / KB;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
@@ -269,8 +272,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           // the leader counts both CTAs' bytes; the peer's copies may land first (the phase
           // cannot complete before the leader's arrival)
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
-          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * BK, mb * 256 + rank * 128);
-          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * BK, nb * C::BN + rank * 128);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, lfull, kb * KB, mb * 256 + rank * 128);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, lfull, kb * KB, nb * C::BN + rank * 128);
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -312,7 +315,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           const uint64_t ad = a_desc0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
           const uint64_t bd = b_desc0 + static_cast<uint64_t>((stage * C::B_BYTES) >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) umma_pair(d_tmem, ad + 2 * k, bd + 2 * k, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // 32 bytes of k a step: 16 bf16 or 32 int8
+            if constexpr (I8)
+              umma_pair_i8(d_tmem, ad + 2 * k, bd + 2 * k, idesc_i8(256, 256), (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_pair(d_tmem, ad + 2 * k, bd + 2 * k, C::IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -446,6 +454,9 @@ static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream
                                      g.M, g.N, g.K, group_m, g.ep, d_status));
 }
 
+static cudaError_t allow_smem_i8() {
+  return cudaFuncSetAttribute(k_gemm2<EPI_I8_F32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Cfg::SMEM);
+}
 template <int BN, int EPI>
 static cudaError_t allow_smem_bn() {
   return cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM);
@@ -464,10 +475,36 @@ int gemm_prepare() {
       allow_smem_bn<256, EPI_QKV>(),     allow_smem_bn<256, EPI_SWIGLU>(), allow_smem_bn<64, EPI_PROJ>(),
       allow_smem_bn<256, EPI_GATE_RESID>(), allow_smem_bn<128, EPI_GATE_RESID>(), allow_smem_bn<256, EPI_F32>(),
       allow_smem_bn<64, EPI_F32>(),      allow_smem_bn<256, EPI_BF16>(),  allow_smem_bn<64, EPI_BF16>(),
-      allow_smem_bn<256, EPI_GELU_BF16>()};
+      allow_smem_bn<256, EPI_GELU_BF16>(), allow_smem_i8()};
   for (cudaError_t x : e)
     if (x != cudaSuccess) return static_cast<int>(x);
   return 0;
+}
+
+// C[M x N] f32 = (A . B^T) * sa[row] * sb[col] with A [M][K] and B [N][K] int8 (tcgen05 kind::i8 on
+// CTA pairs); the scales are g.ep.mod (A's rows) and g.ep.norm_q (B's rows)
+int gemm_i8_launch(const GemmArgs& g, const int8_t* a, const int8_t* b, int* d_status, int num_sms, cudaStream_t st) {
+  using C = Gemm2Cfg;
+  if (g.M <= 0 || g.N % 256 || g.K % 128 || g.K <= 0 || num_sms < 2) return -1;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) return -1;
+  CUtensorMap ta, tb;
+  const uint64_t da[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.M)};
+  const uint64_t sa[1] = {static_cast<uint64_t>(g.K)};
+  const uint32_t ba[2] = {128, 128};
+  const uint64_t db[2] = {static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(g.K)};
+  if (make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, 2, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, 2, db, sb, ba, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -4;
+  const int num_m = (g.M + 255) / 256;
+  const int tiles = num_m * (g.N / C::BN);
+  int clusters = num_sms / 2;
+  clusters = tiles < clusters ? tiles : clusters;
+  int group_m = static_cast<int>((48ll << 20) / (256ll * g.K));
+  group_m = group_m < 4 ? 4 : group_m;
+  group_m = group_m > num_m ? num_m : group_m;
+  return static_cast<int>(launch_pdl(k_gemm2<EPI_I8_F32, true>, dim3(clusters * 2), dim3(GEMM_THREADS), C::SMEM, st,
+                                     ta, tb, g.M, g.N, g.K, group_m, g.ep, d_status));
 }
 
 int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {

@@ -92,6 +92,25 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
         store_bf16x32(static_cast<bf16*>(e.out) + orow * e.ld_out + col0 + c, f);
       }
     }
+  } else if constexpr (EPI == EPI_I8_F32) {
+    // s32 accumulators of an int8 product, scaled by A's row scale (e.mod) and B's row scales (e.norm_q)
+    const float sr = valid ? __ldg(e.mod + row) : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c, r);
+      if (!valid) continue;
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + static_cast<long long>(row) * e.ld_out + col0 + c);
+      const float4* sc = reinterpret_cast<const float4*>(e.norm_q + col0 + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 s4 = __ldg(sc + i);
+        o[i] = make_float4(__int2float_rn(static_cast<int>(r[4 * i])) * sr * s4.x,
+                           __int2float_rn(static_cast<int>(r[4 * i + 1])) * sr * s4.y,
+                           __int2float_rn(static_cast<int>(r[4 * i + 2])) * sr * s4.z,
+                           __int2float_rn(static_cast<int>(r[4 * i + 3])) * sr * s4.w);
+      }
+    }
   } else if constexpr (EPI == EPI_GATE_RESID) {
     const int t = row % e.seg_in;
     const float* g = e.mod + (e.n0 + t < e.p ? e.mod_stride : 0) + col0;

@@ -7,7 +7,7 @@
 // computes 256 x 256 tiles with tcgen05.mma.cta_group::2 exactly as k_gemm2
 // does; what changes is where B comes from.  Per 64-deep k-block each CTA's TMA
 // producer brings its 128 rows of A (bf16, 128B swizzle) and its half of B as
-// int8 (128 rows x 64 bytes) with the two fp16 scales of each row; four
+// int8 (128 rows x 64 bytes) with the two fp16 scales of each row; eight
 // converter warps then write B as bf16 into the 128B-swizzled operand layout a
 // TMA load would have produced (row r's 16-byte chunk j at chunk j ^ (r % 8)),
 // computing each value as round-to-nearest bf16 of (float) q * (float) d: the
@@ -18,9 +18,10 @@
 //               (on this CTA's qfull barrier)
 //   warp 1      MMA issue (leader only)
 //   warps 2..5  epilogue (as k_gemm2)
-//   warps 6..9  int8 -> bf16 conversion into the stage's B buffer
+//   warps 6..13 int8 -> bf16 conversion into the stage's B buffer, a pair of
+//               warps per k-block, four k-blocks at once
 // The leader's full barrier of a stage completes when both CTAs' A bytes have
-// landed and both CTAs' converters have arrived.  No multicast loads.
+// landed and both CTAs' two converter warps have arrived.  No multicast loads.
 #include "gemm_common.cuh"
 
 namespace exn {
@@ -32,7 +33,8 @@ struct Gemm2QCfg {
   static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's half of B, converted to bf16
   static constexpr int Q_BYTES = 128 * BK;      // the same half as int8
   static constexpr int D_BYTES = 128 * 2 * 2;   // its fp16 scales: two 32-blocks per row
-  static constexpr int THREADS = 320;
+  static constexpr int CONV = 8;                // converter warps: 4 pairs, a pair per k-block in flight
+  static constexpr int THREADS = 32 * (6 + CONV);
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES + Q_BYTES + D_BYTES) + 1024 + 256;
   static constexpr uint32_t IDESC = idesc_bf16(256, 256);
@@ -90,7 +92,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2QCfg::THREADS, 
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 3);   // the leader's producer (A bytes of both CTAs) + one converter per CTA
+      mbar_init(&full[s], 5);   // the leader's producer (A bytes of both CTAs) + two converter warps per CTA
       mbar_init(&empty[s], 1);  // the leader's multicast commit
       mbar_init(&qfull[s], 1);  // this CTA's producer (int8 and scale bytes)
     }
@@ -216,16 +218,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2QCfg::THREADS, 
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
     }
   } else {
-    // ---- converter warps 6..9: warp w converts every fourth k-block (iterations i with i % 4 == w) whole,
-    // so four stages convert at once and each warp's chain (wait, convert, fence, arrive) overlaps the
-    // others'.  Lane l takes the 16-byte pieces c = l + 32 j (j < 16), row c / 4, k 16 (c % 4) .. +15:
-    // each int8 load of the warp covers 512 contiguous bytes, each bf16 store 32 bank-spread chunks.
-    const int cw = warp - 6;
+    // ---- converter warps 6..13: pair p = (w - 6) / 2 converts the k-blocks i with i % 4 == p, its two
+    // warps half the rows each, so four k-blocks convert at once and each warp's chain (wait, convert,
+    // fence, arrive) overlaps the others'.  Lane l takes the 16-byte pieces c = l + 32 j (j < 8) of its
+    // 64 rows, row 64 h + c / 4, k 16 (c % 4) .. +15: each int8 load of the warp covers 512 contiguous
+    // bytes, each bf16 store 32 bank-spread chunks of the 128-byte-swizzled layout.
+    const int cw = warp - 6, pair = cw >> 1, half = cw & 1;
     bool ok = true;
     int it = 0;
     for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
-        if ((it & 3) != cw) continue;
+        if ((it & 3) != pair) continue;
         const int stage = it % C::STAGES;
         const uint32_t phase = static_cast<uint32_t>(it / C::STAGES) & 1;
         if (!(ok = mbar_wait_uniform(&qfull[stage], phase, abort_flag, status, STATUS_TIMEOUT_GEMM))) break;
@@ -233,9 +236,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2QCfg::THREADS, 
         const __half* d = reinterpret_cast<const __half*>(sD + stage * C::D_BYTES);
         uint8_t* b = sB + stage * C::B_BYTES;
 #pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const int c = lane + 32 * j;
-          const int row = c >> 2, seg = c & 3;
+          const int row = 64 * half + (c >> 2), seg = c & 3;
           const int4 qv = *reinterpret_cast<const int4*>(q + row * 64 + seg * 16);
           const float dv = __half2float(d[row * 2 + (seg >> 1)]);
           uint32_t o[8];

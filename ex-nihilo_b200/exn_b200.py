@@ -97,10 +97,14 @@ def lib():
         "exn_test_gemm": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_gemm_q8": (ctypes.c_int, [H, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.POINTER(ctypes.c_double)]),
+        "exn_test_gemm_i8": (ctypes.c_int, [H, vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.POINTER(ctypes.c_double)]),
         "exn_test_gemm_timed": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.POINTER(ctypes.c_double)]),
         "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
         "exn_test_gemm_pairs": (ctypes.c_int, [H, ctypes.c_int]),
+        "exn_test_comm_stats": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong),
+                                               ctypes.POINTER(ctypes.c_double)]),
         "exn_test_attention_split": (ctypes.c_int, [H, ctypes.c_int, ctypes.c_int]),
         "exn_test_ln_mod": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "exn_test_qkv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6),
@@ -290,6 +294,12 @@ class Dit:
 
     def launch_count(self):
         return int(lib().exn_test_launch_count(self.h))
+
+    def comm_stats(self):
+        """(waits for a queued NCCL call, 50 us sleeps in them, seconds) since open."""
+        n, z, t = ctypes.c_longlong(), ctypes.c_longlong(), ctypes.c_double()
+        self._ck(lib().exn_test_comm_stats(self.h, ctypes.byref(n), ctypes.byref(z), ctypes.byref(t)))
+        return n.value, z.value, t.value
 
     def last_call_ms(self):
         """Device time of the last velocity / generate call, inputs in HBM (ms)."""

@@ -26,6 +26,13 @@ int exn_test_gemm(exn_handle* h, const void* a, const void* b, float* c, int m, 
 int exn_test_gemm_q8(exn_handle* h, const void* a, const void* qs, const void* d, float* c, int m, int n, int k,
                      int reps, double* ms);
 
+/* C[m x n] f32 = (A . B^T) * SA[row] * SB[col] with A [m][k] and B [n][k] int8 (tcgen05 kind::i8,
+ * s32 accumulation, CTA pairs): the W8A8 form of the reference's *int8* path (src/cuda-dit.lisp
+ * :110-126) with one scale per activation row and per weight row; n a multiple of 256, k of 128.
+ * REPS and MS as exn_test_gemm_q8. */
+int exn_test_gemm_i8(exn_handle* h, const void* a, const void* b, const float* sa, const float* sb, float* c, int m,
+                     int n, int k, int reps, double* ms);
+
 /* exn_test_gemm run REPS times back to back; *MS the mean time of one (CUDA events). */
 int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, int m, int n, int k, int reps,
                         double* ms);
@@ -34,6 +41,11 @@ int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, i
  * q [batch][nq][heads*128], k/v [batch][kv_rows][heads*128], out like q. */
 int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                        int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
+
+/* Host side of the communicator waits since the handle was opened: how many times the library
+ * waited for an NCCL call to be queued (every barrier of a sequence-parallel pass does), how many
+ * 50 us sleeps those waits took, and their total wall time in seconds. */
+int exn_test_comm_stats(exn_handle* h, long long* settles, long long* sleeps, double* seconds);
 
 /* The GEMM tiles of this handle's later calls: PAIRS 1 (the default) 256 x 256 tiles on CTA pairs
  * wherever N is a multiple of 256, 0 128-row tiles of one CTA everywhere. */

@@ -86,6 +86,31 @@ def test_gemm_q8_equals_the_bf16_slab(dit, m, n, k):
     assert torch.equal(c0, c1)
 
 
+@pytest.mark.parametrize("m,n,k", [(100, 256, 128), (300, 512, 384), (1000, 768, 4096)])
+def test_gemm_i8_matches_exact_integer_product(dit, m, n, k):
+    """The int8 (kind::i8) GEMM: s32 accumulation is exact, so with unit scales it equals the integer
+    product exactly, and with scales it is that product times sa[row] sb[col] (fp32 roundings only)."""
+    g = torch.Generator().manual_seed(m + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int32)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int32)
+    exact = (a.double() @ b.double().T)
+    sa = torch.rand(m, generator=g) + 0.5
+    sb = torch.rand(n, generator=g) + 0.5
+    ad, bd = a.to(torch.int8).cuda(), b.to(torch.int8).cuda()
+    for scaled in (False, True):
+        s_a = (sa if scaled else torch.ones(m)).float().cuda()
+        s_b = (sb if scaled else torch.ones(n)).float().cuda()
+        c = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+        dit._ck(E.lib().exn_test_gemm_i8(dit.h, ad.data_ptr(), bd.data_ptr(), s_a.data_ptr(), s_b.data_ptr(),
+                                         c.data_ptr(), m, n, k, 0, None))
+        want = exact * s_a.double().cpu()[:, None] * s_b.double().cpu()[None, :]
+        got = c.double().cpu()
+        if scaled:
+            assert ((got - want).abs() / want.abs().clamp_min(1.0)).max().item() < 1e-6
+        else:
+            assert torch.equal(got, exact.float().double())   # the exact s32 sum, rounded once to fp32
+
+
 def attention_ref(q, k, v, q0, p, l, b0, b1, heads):
     """fp64 masked softmax attention on the (already bf16-rounded) inputs."""
     qq = q.double().reshape(q.shape[0], heads, 128)
