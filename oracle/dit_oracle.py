@@ -152,6 +152,12 @@ def synth_unit(seed: int, stream: int, count: int, start: int = 0) -> np.ndarray
     terms) and centred.  Returned as the exact integer offsets (int32); the
     float value is ``offset * scale`` with ``scale`` a float32 constant, so the
     CUDA generator reproduces every bit."""
+    chunk = 1 << 20
+    if count > chunk:  # in cache-sized pieces: the same values, twice as fast for large tensors
+        out = np.empty(count, dtype=np.int32)
+        for s in range(0, count, chunk):
+            out[s:s + min(chunk, count - s)] = synth_unit(seed, stream, min(chunk, count - s), start + s)
+        return out
     idx = np.arange(start, start + count, dtype=np.uint64)
     with np.errstate(over="ignore"):
         c = (np.uint64(stream) << np.uint64(32)) | idx
