@@ -90,6 +90,32 @@ def edit_flops(layers=LAYERS, p_text=512, a=8, rh=64, rw=64, h=H, w=WW):
     return gemm1 + 7 * gemm2, attn1 + 7 * attn2
 
 
+def vae_flops(h=H, w=WW):
+    """Algorithmic FLOPs of one VAE decode of an h x w latent (src/cuda-vae.lisp:94-136, the shapes of
+    src/weights.lisp:63-100): 3 x 3 convolutions 18 Cin Cout a pixel, 1 x 1 ones 2 Cin Cout, the
+    middle attention's two products 4 n^2 c."""
+    stages = ((1152, 1152, True), (1152, 1152, True), (1152, 576, True), (576, 288, True), (288, 144, False))
+    n, top = h * w, 1152
+    f = 2.0 * 64 * 64 * n + 18.0 * 64 * top * n                     # conv2, decoder.conv1
+    res = lambda i, o, n: 18.0 * n * (i * o + o * o) + (2.0 * i * o * n if i != o else 0.0)
+    f += 2 * res(top, top, n) + 2.0 * n * top * 3 * top + 4.0 * n * n * top + 2.0 * n * top * top
+    for i, o, up in stages:
+        f += res(i, o, n) + 2 * res(o, o, n)
+        if up:
+            n *= 4
+            f += 18.0 * o * o * n
+    return f + 18.0 * 144 * 4 * n
+
+
+def peak_clock_mhz():
+    """The median SM clock under load while MEASURED_PEAKS.json's sustained peak was measured."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["clocks_under_load"]["sm_mhz_median"])
+    except Exception:
+        return None
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -350,6 +376,7 @@ def run_exn(args):
         d.close()
         return None
     bt_burst, bt, hbm, src = peaks()     # the kernels run inside a long step: the sustained figure
+    clk_mhz = clk.summary()["sm_mhz"]
     gf, af = picture_flops(len(groups[0]), args.layers)      # the profiled picture batch
     total_units = args.pictures if args.workload == "cfg5" else world * B
     value = total_units * 1e3 / ms
@@ -387,6 +414,11 @@ def run_exn(args):
                                "largest kernel, 32% of a picture's kernel time)",
                      "achieved": round(gu_tflops, 1) if gu_tflops else None, "peak": bt, "unit": "TFLOP/s",
                      "frac": round(gu_tflops / bt, 4) if gu_tflops else None,
+                     "frac_clock_normalised": (round(gu_tflops * peak_clock_mhz() / clk_mhz / bt, 4)
+                                               if gu_tflops and clk_mhz and peak_clock_mhz() else None),
+                     "clock_note": "frac_clock_normalised = achieved x (the peak's median SM MHz %s / this run's %s) "
+                                   "/ peak: the same kernel at the clock the peak was measured at"
+                                   % (peak_clock_mhz(), clk_mhz),
                      "traffic": GATEUP_TRAFFIC,
                      "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at the first "
                                      "step's 4224 rows; algorithmic bytes %.4g" % GATEUP_ALG_BYTES,
@@ -414,6 +446,26 @@ def run_exn(args):
         out["config"]["global_batch"] = args.pictures
     if args.layers != LAYERS:
         out["config"]["workload"] += " -- PROFILING CASE with %d of 32 blocks, not a bench number" % args.layers
+    # the step after the DiT: the VAE decoder on one picture's latent (rank 0, 1 GPU lines only)
+    if world == 1 and not args.no_vae:
+        v = E.Vae(device=local)
+        v.load_synthetic(1)
+        zl = (lat_h[0] * 0.5).astype(np.float32)
+        for _ in range(2):
+            v.decode(zl, H, WW)
+        vm = []
+        for _ in range(3):
+            rgba = v.decode(zl, H, WW)
+            vm.append(v.last_ms())
+        v.close()
+        vf = vae_flops()
+        out["vae_decode"] = {"workload": "VAE decoder (Wan 2.2, one frame): 64 x 64 latent -> 1024 x 1024 RGBA",
+                             "ms": round(min(vm), 3), "algorithmic_tflop": round(vf / 1e12, 3),
+                             "tflops": round(vf / (min(vm) * 1e-3) / 1e12, 1),
+                             "frac": round(vf / (min(vm) * 1e-3) / 1e12 / bt, 4),
+                             "finite": bool(np.isfinite(rgba).all()),
+                             "timing": "CUDA events on the decoder's stream, latent upload to pixel download, best "
+                                       "of 3 after 2 warm-up decodes; synthetic bf16 weights"}
     if world == 1 and not args.no_cpu:
         with all_host_threads():
             bs = cpu_block_seconds()
@@ -555,6 +607,7 @@ def main():
                     help="cfg2: one picture per GPU per step (default); cfg4: one 8704-row edit over all GPUs; "
                          "cfg5: 64 pictures split over the GPUs")
     ap.add_argument("--pictures", type=int, default=64, help="cfg5: pictures in the job")
+    ap.add_argument("--no-vae", action="store_true", help="skip the VAE decoder timing (1 GPU lines)")
     ap.add_argument("--no-sp-edit", action="store_true",
                     help="N > 1: skip the config-4 edit shared by all GPUs that follows the replica timing")
     args = ap.parse_args()

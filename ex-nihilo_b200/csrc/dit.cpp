@@ -157,8 +157,10 @@ struct SpBufs {
   float2* rope = nullptr;    // RoPE of this rank's rows [n_loc][64]
   float* zslice = nullptr;   // [64][N/G]
   float* zall = nullptr;     // [G][64][N/G]
-  int* bar = nullptr;        // one int the pass's barriers all-reduce
-  size_t off_qf = 0, off_att = 0;
+  int* bar = nullptr;        // one int the set-up barriers all-reduce
+  int* flags = nullptr;      // [kMaxSp]: slot g holds the last barrier epoch rank g arrived at (peers write it)
+  int epoch = 0;             // barriers of the passes taken since the buffers were made (the same on every rank)
+  size_t off_qf = 0, off_att = 0, off_flags = 0;
   bf16* kv = nullptr;        // [layer][K or V][L][Wg]: this rank's heads of the whole sequence
   int kv_l = 0;
   // every rank's mem and kv mapped into this process (CUDA IPC; this rank's own at its index)
@@ -792,6 +794,24 @@ int sp_barrier(exn_handle* h, const char* what) {
   return nccl_settle(h, h->comm, what);
 }
 
+// A barrier of the pass on the device: a one-block kernel stores this barrier's epoch into every
+// rank's arrival slot for this rank (peer memory over NVLink, release at system scope) and waits,
+// bounded, until every rank's slot here holds it.  What a rank's kernels stored into peers before it
+// (each writer fences at system scope) is then visible to every rank's kernels after it.  The host
+// only queues it: unlike a collective of a non-blocking communicator it never waits for the enqueue.
+int sp_flag_barrier(exn_handle* h) {
+  SpBufs& b = h->sp;
+  SpFlags f;
+  for (int g = 0; g < kMaxSp; ++g)
+    f.peer[g] = g < h->world ? reinterpret_cast<int*>(b.peer_mem[g] + b.off_flags) + h->rank : nullptr;
+  f.mine = b.flags;
+  ++b.epoch;
+  ++h->launches;
+  const int r = sp_flag_barrier_launch(f, h->world, b.epoch, h->d_status, h->st);
+  if (r) return fail(h, EXN_ECUDA, "pass barrier launch failed: %d", r);
+  return EXN_OK;
+}
+
 // Unmap the peers' buffers (after this rank's queued work is done).
 void sp_unmap(exn_handle* h) {
   SpBufs& b = h->sp;
@@ -875,7 +895,8 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
     };
     const size_t oxp = take(size_t(std::max(PP, 1)) * W * 4), oqf = take(size_t(NT) * Wg * 2),
                  oat = take(size_t(NL) * W * 2), orp = take(size_t(NL) * 64 * 8),
-                 ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4), obar = take(sizeof(int));
+                 ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4), obar = take(sizeof(int)),
+                 oflg = take(kMaxSp * sizeof(int));
     if (b.mem) cudaFree(b.mem);
     b.mem = nullptr;
     CK(cudaMalloc(&b.mem, off));
@@ -887,8 +908,12 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
     b.zslice = reinterpret_cast<float*>(m + ozs);
     b.zall = reinterpret_cast<float*>(m + oza);
     b.bar = reinterpret_cast<int*>(m + obar);
+    b.flags = reinterpret_cast<int*>(m + oflg);
+    CK(cudaMemsetAsync(b.flags, 0, kMaxSp * sizeof(int), h->st));  // before the exchange that lets peers write
+    b.epoch = 0;
     b.off_qf = oqf;
     b.off_att = oat;
+    b.off_flags = oflg;
     b.cap_nloc = NL;
     b.cap_ntot = NT;
     b.cap_p = PP;
@@ -1018,7 +1043,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     eq.sp_p = P;
     if ((rc = gemm(h, h->y, W, h->w_qkv + static_cast<size_t>(il) * 3 * W * W, W, n_loc, 3 * W, W, EPI_QKV, eq)))
       return rc;
-    if ((rc = sp_barrier(h, "barrier before attention"))) return rc;
+    if ((rc = sp_flag_barrier(h))) return rc;
     AttnArgs aa;
     aa.q = b.qf;
     aa.k = b.kv + kl_off;
@@ -1045,7 +1070,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     aa.sp_nl = Nl;
     aa.sp_img0 = img0;
     if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
-    if ((rc = sp_barrier(h, "barrier after attention"))) return rc;
+    if ((rc = sp_flag_barrier(h))) return rc;
     GemmEpi eo;
     eo.out = h->x;
     eo.ld_out = W;

@@ -406,6 +406,30 @@ __global__ void k_wait_probe(int* status, unsigned long long limit_ns) {
   if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, STATUS_TIMEOUT_PROBE, limit_ns);
 }
 
+// One thread per rank g: store EPOCH into rank g's slot for this rank, then wait until rank g's
+// arrival here shows EPOCH (epochs only grow).  Bounded: after LIMIT_NS the thread records
+// STATUS_TIMEOUT_COMM and stops waiting, so a rank that died ends the pass with an error.
+__global__ void k_sp_flag_barrier(const SpFlags f, int world, int epoch, int* status, unsigned long long limit_ns) {
+  const int g = threadIdx.x;
+  if (g < world) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f.peer[g]), "r"(epoch) : "memory");
+    const uint64_t t0 = globaltimer();
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(f.mine + g) : "memory");
+      if (v >= epoch) break;
+      if (globaltimer() - t0 > limit_ns) {
+        atomicOr(status, STATUS_TIMEOUT_COMM);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
 // destination row of weight row r: gate_up interleaved by 128 when ilv (= FFN) > 0
 __device__ __forceinline__ long long dst_row(long long r, long long row0, int ilv) {
   if (ilv <= 0) return row0 + r;
@@ -647,6 +671,12 @@ void digest_launch(const void* p, size_t bytes, unsigned long long* out, cudaStr
   if (n <= 0) return;
   k_digest<<<static_cast<unsigned>(n < 148LL * 2048 ? blocks_for(n, 256) : 148 * 8), 256, 0, st>>>(
       static_cast<const uint64_t*>(p), n, out);
+}
+
+int sp_flag_barrier_launch(const SpFlags& f, int world, int epoch, int* status, cudaStream_t st) {
+  if (world < 1 || world > kMaxSp) return -1;
+  k_sp_flag_barrier<<<1, 32, 0, st>>>(f, world, epoch, status, 4000000000ull);
+  return static_cast<int>(cudaGetLastError());
 }
 
 void wait_probe_launch(int* status, unsigned long long limit_ns, cudaStream_t st) {

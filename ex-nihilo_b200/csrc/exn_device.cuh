@@ -26,6 +26,7 @@ enum : int {
   STATUS_TIMEOUT_ATTN = 2,
   STATUS_BAD_ARG = 4,
   STATUS_TIMEOUT_PROBE = 8,  // the test kernel whose wait is meant to run out
+  STATUS_TIMEOUT_COMM = 16,  // a pass barrier whose peers did not all arrive
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -312,6 +313,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" : EXN_U8(0), EXN_U8(8), EXN_U8(16), EXN_U8(24)::"memory");
+}
+
+// 32 lanes x 16 columns
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : EXN_R8(0), EXN_R8(8)
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : EXN_U8(0), EXN_U8(8)::"memory");
 }
 
 // 32 lanes x 64 columns in one instruction

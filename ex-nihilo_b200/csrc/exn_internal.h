@@ -140,6 +140,60 @@ int q8_scales_by_kblock_launch(const __half* d, __half* out, int n, int k, cudaS
 constexpr int kNoAllocMaxRows = 8704;
 int noalloc_rope_scratch(int device, float2** table);
 
+// A barrier of the sequence-parallel group on the device (elementwise.cu): PEER[g] is rank g's
+// arrival slot for this rank (peer memory), MINE this rank's slots [WORLD].  The kernel stores EPOCH
+// into every PEER[g] and waits (bounded, 4 s; then STATUS_TIMEOUT_COMM into *status) until every
+// MINE[g] >= EPOCH.  0 or a cudaError_t.
+struct SpFlags {
+  int* peer[kMaxSp];
+  int* mine;
+};
+int sp_flag_barrier_launch(const SpFlags& f, int world, int epoch, int* status, cudaStream_t st);
+
+// --- the VAE decoder's convolutions (conv.cu): implicit GEMM over channels-last bf16 pictures ---
+enum ConvKind : int {
+  CONV_F32 = 0,   // out f32 [pixel][ld_out] = acc + bias (+ res [pixel][ld_res])
+  CONV_BF16 = 1,  // out bf16 [pixel][ld_out] = acc + bias
+  CONV_RGBA = 2,  // out f32 [pixel][4] = clamp(acc + bias, -1, 1) of the first 4 channels
+};
+struct ConvEpi {
+  int kind = CONV_F32;
+  void* out = nullptr;
+  long long ld_out = 0;
+  const float* bias = nullptr;  // [cout rounded up to 16]
+  const float* res = nullptr;
+  long long ld_res = 0;
+  int cout = 0;                 // set by conv_launch
+};
+struct ConvArgs {
+  const bf16* x = nullptr;   // [h][w][cp]: channels padded to a multiple of 64 with zeros
+  const bf16* wt = nullptr;  // [cout tiles x BN][taps][cp]: tap-major rows of weights, zero padding
+  int h = 0, w = 0, cp = 0, cout = 0, taps = 9;
+  ConvEpi ep;
+};
+int conv_launch(const ConvArgs& a, int* d_status, int num_sms, cudaStream_t st);
+int conv_prepare();
+// rows of the weight matrix conv_launch wants for COUT output channels (a multiple of its tile)
+inline int conv_rows(int cout) { return cout % 144 == 0 ? cout : (cout % 64 == 0 ? cout : (cout + 15) / 16 * 16); }
+
+// --- the VAE decoder's memory-bound kernels (vae.cu) ---
+// y bf16 [n][cp] = (silu)(x / max(|x|, 1e-12) * sqrt(c) * gamma) of x f32 [n][c]; channels c.. cp-1 zero
+void vae_norm_launch(const float* x, const float* gamma, bf16* y, int n, int c, int cp, int silu, cudaStream_t st);
+// v = bf16-rounded v (round to nearest even), in place
+void round_bf16_launch(float* v, long long n, cudaStream_t st);
+// y bf16 [n][cp] = x f32 [n][c]; channels c.. cp-1 zero
+void vae_to_bf16_launch(const float* x, bf16* y, long long n, int c, int cp, cudaStream_t st);
+// u bf16 [2h][2w][cp]: x f32 [h][w][c] repeated 2 x 2 (nearest), channels c.. cp-1 zero
+void vae_up2_launch(const float* x, bf16* u, int h, int w, int c, int cp, cudaStream_t st);
+// y f32 [2h][2w][co] += DupUp3D(keep f32 [h][w][ci]) of the last of FT frames
+void vae_dupup_add_launch(const float* keep, float* y, int h, int w, int ci, int co, int ft, cudaStream_t st);
+// p bf16 [n][n] = softmax(s * scale) by rows of s f32 [n][n]
+void vae_softmax_launch(const float* s, bf16* p, int n, float scale, cudaStream_t st);
+// out bf16 [c][n] = in bf16 [n][c] (row stride ld_in)
+void vae_transpose_launch(const bf16* in, long long ld_in, bf16* out, int n, int c, cudaStream_t st);
+// a conv weight [o][i][taps] (f32) -> bf16 [rows][taps][cp], rows >= o and channels >= i zero
+void vae_weight_launch(const float* w, bf16* out, int o, int i, int taps, int rows, int cp, cudaStream_t st);
+
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.
 // single: one modulation row for every row (norm_out's scale).

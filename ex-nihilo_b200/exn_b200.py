@@ -89,6 +89,15 @@ def lib():
         "exn_generate_device": (ctypes.c_int, [H, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int,
                                                ctypes.POINTER(ctypes.c_double), ctypes.c_int, vp]),
         "exn_sync": (ctypes.c_int, [H]),
+        "exn_vae_open": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(H)]),
+        "exn_vae_close": (None, [H]),
+        "exn_vae_last_error": (ctypes.c_char_p, [H]),
+        "exn_vae_load_safetensors": (ctypes.c_int, [H, ctypes.c_char_p]),
+        "exn_vae_load_synthetic": (ctypes.c_int, [H, ctypes.c_uint64]),
+        "exn_vae_weights_ready": (ctypes.c_int, [H]),
+        "exn_vae_decode": (ctypes.c_int, [H, fp, ctypes.c_int, ctypes.c_int, fp]),
+        "exn_vae_release": (ctypes.c_int, [H]),
+        "exn_test_vae_last_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
         "exn_release": (ctypes.c_int, [H]),
         "exn_comm_unique_id": (ctypes.c_int, [vp]),
         "exn_comm_init": (ctypes.c_int, [H, vp, ctypes.c_int, ctypes.c_int]),
@@ -308,6 +317,59 @@ class Dit:
         return ms.value
 
 
+class Vae:
+    """The VAE decoder on one CUDA device: the reference's GVAE structure (src/cuda-vae.lisp:10-13)."""
+
+    def __init__(self, device=0):
+        h = ctypes.c_void_p()
+        rc = lib().exn_vae_open(device, ctypes.byref(h))
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_vae_last_error(None).decode(errors="replace"))
+        self.h = h
+
+    def _ck(self, rc):
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_vae_last_error(self.h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().exn_vae_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def load_safetensors(self, path):
+        self._ck(lib().exn_vae_load_safetensors(self.h, str(path).encode()))
+
+    def load_synthetic(self, seed=1):
+        self._ck(lib().exn_vae_load_synthetic(self.h, seed))
+
+    def decode(self, latent, h, w):
+        """LATENT (64 x h x w, denormalised) -> RGBA (16h, 16w, 4) in -1 .. 1."""
+        z = _f32(latent, (64, h, w))
+        out = np.empty((16 * h, 16 * w, 4), dtype=np.float32)
+        self._ck(lib().exn_vae_decode(self.h, _fp(z), h, w, _fp(out)))
+        return out
+
+    def release(self):
+        self._ck(lib().exn_vae_release(self.h))
+
+    def last_ms(self):
+        ms = ctypes.c_double()
+        self._ck(lib().exn_test_vae_last_ms(self.h, ctypes.byref(ms)))
+        return ms.value
+
+
 # ---- the reference's names
 
 def upload_dit(path, device=0, **shape) -> Dit:
@@ -334,3 +396,24 @@ def dit_release(d: Dit):
 def euler_steps(d: Dit, context, p, z, h, w, sigmas=TURBO_SIGMAS, prefix_key=None, ref=None):
     """generate's loop (src/generate.lisp:133-135) with the update fused on the device."""
     return d.generate(context, p, z, h, w, sigmas, prefix_key=prefix_key, ref=ref)
+
+
+def upload_vae(path, device=0) -> Vae:
+    """(upload-vae path :device device), src/cuda-vae.lisp:15-27 (the decoder's tensors)."""
+    v = Vae(device)
+    try:
+        v.load_safetensors(path)
+    except Exception:
+        v.close()
+        raise
+    return v
+
+
+def vae_decode(v: Vae, latent, h, w):
+    """(vae-decode v latent h w), src/cuda-vae.lisp:94-136: RGBA rows, channels last."""
+    return v.decode(latent, h, w)
+
+
+def vae_release(v: Vae):
+    """(vae-release v), src/cuda-vae.lisp:29-33."""
+    v.release()

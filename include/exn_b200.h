@@ -153,6 +153,40 @@ int exn_comm_unique_id(void* id128);  /* 128 bytes: rank 0 makes it, every rank 
 int exn_comm_init(exn_handle* h, const void* id128, int rank, int world);
 int exn_comm_destroy(exn_handle* h);
 
+/* ---- The VAE decoder: a latent to RGBA pixels (Wan 2.2's decoder, one frame, 2-D), the step
+ * after the DiT.  Each entry point replaces one function of src/cuda-vae.lisp:
+ *
+ *   exn_vae_open + exn_vae_load_safetensors
+ *                      (upload-vae path :device d)   src/cuda-vae.lisp:15-27, with open-vae's
+ *                      checks of the decoder's tensors (src/weights.lisp:67-100, 116-127)
+ *   exn_vae_decode     (vae-decode v latent h w)      src/cuda-vae.lisp:94-136
+ *   exn_vae_release    (vae-release v)                src/cuda-vae.lisp:29-33
+ *
+ * Same conventions as the DiT's handle (int status, exn_vae_last_error).  Convolutions run on the
+ * tensor cores with bf16 operands and fp32 accumulation; the weights are the checkpoint's bf16. */
+typedef struct exn_vae exn_vae;
+
+int exn_vae_open(int device, exn_vae** out);
+void exn_vae_close(exn_vae* v);
+const char* exn_vae_last_error(const exn_vae* v);
+
+/* The decoder's tensors from a safetensors file (BF16 or F32), each checked by name and shape;
+ * tensors the decoder does not use (the encoder's) are ignored. */
+int exn_vae_load_safetensors(exn_vae* v, const char* path);
+
+/* Every decoder tensor from the deterministic synthetic generator (weights N(0, 1/fan_in), biases
+ * N(0, 0.02), gains 1 + N(0, 0.1), all rounded to bf16), the same bits as the test oracle's. */
+int exn_vae_load_synthetic(exn_vae* v, uint64_t seed);
+int exn_vae_weights_ready(const exn_vae* v);
+
+/* vae-decode: LATENT (64 x h x w floats, channel-major, denormalised) to RGBA (16h x 16w x 4
+ * floats, -1 .. 1, row-major, channels last).  h x w must be a multiple of 64 (1024 x 1024: a
+ * 64 x 64 latent; 1536 x 1024: 64 x 96). */
+int exn_vae_decode(exn_vae* v, const float* latent, int h, int w, float* rgba);
+
+/* vae-release: the decoder's scratch freed (the weights stay). */
+int exn_vae_release(exn_vae* v);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,6 +3,8 @@ numpy DiT, ``inspect/ref_dit.py`` of ex-nihilo, on synthetic inputs.
 
     python tests/golden/make_golden.py --ref-dir <ex-nihilo>/inspect [--full]
 
+The DiT cases run ``inspect/ref_dit.py``; the VAE case (``vae_small``) runs ``inspect/ref_vae.py``.
+
 For each case it
 
 1. makes the synthetic DiT with ``oracle.dit_oracle.SynthWeights`` (Q8_0),
@@ -57,6 +59,37 @@ FULL = {
     # 1536 x 1024 (a 64 x 96 latent, a non-square RoPE grid), 256 text rows, 8 steps
     "cfg3_euler": dict(shape=dict(), p=256, h=64, w=96, euler=True),
 }
+
+
+VAE_CASES = {
+    # the decoder on an 8 x 8 latent (a 128 x 128 picture): every stage, the middle attention over 64 pixels
+    "vae_small": dict(h=8, w=8),
+}
+
+
+def run_vae_case(ref_dir, name, case, outdir):
+    """The reference's own inspect/ref_vae.py decoding a synthetic latent with the oracle's synthetic
+    decoder weights, written as a real BF16 safetensors file and read back through ref_vae's ST."""
+    from oracle import vae_oracle as V
+    spec = importlib.util.spec_from_file_location("ref_vae", os.path.join(ref_dir, "ref_vae.py"))
+    RV = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(RV)
+    t0 = time.time()
+    sw = V.SynthVae(1)
+    z = O.synth_normal(0, 3000, (64, case["h"], case["w"]))
+    h = hashlib.sha256()
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "vae.safetensors")
+        V.write_safetensors(path, [(n, sw(n)) for n, _ in sw.spec])
+        for n, _ in sw.spec:
+            h.update(sw(n).tobytes())
+        with contextlib.redirect_stdout(io.StringIO()):
+            rgba = RV.decode(RV.ST(path), z)
+    np.savez(os.path.join(outdir, name + ".npz"), rgba=rgba,
+             meta=json.dumps(dict(case=name, h=case["h"], w=case["w"], weight_seed=1, latent="synth_normal(0, 3000)",
+                                  reference="inspect/ref_vae.py decode, BF16 safetensors")),
+             weights_sha256=np.array(h.hexdigest()), latent_sha256=np.array(hashlib.sha256(z.tobytes()).hexdigest()))
+    print("%s: %.1fs" % (name, time.time() - t0), flush=True)
 
 
 def load_ref(ref_dir):
@@ -142,6 +175,10 @@ def main():
         if args.only and name not in args.only.split(","):
             continue
         run_case(R, name, case, HERE)
+    for name, case in VAE_CASES.items():
+        if args.only and name not in args.only.split(","):
+            continue
+        run_vae_case(args.ref_dir, name, case, HERE)
 
 
 if __name__ == "__main__":

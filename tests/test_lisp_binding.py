@@ -1,16 +1,17 @@
-"""The Lisp binding (lisp/b200-dit.lisp) against the C header it binds.
+"""The Lisp bindings (lisp/b200-dit.lisp, lisp/b200-vae.lisp) against the C header they bind.
 
 SBCL is not installed here, so the binding cannot run; these checks read it as
 text: the file is balanced s-expressions, every sb-alien routine names a
 function that include/exn_b200.h declares, with the same number of arguments
 and the same kind of each argument and result, the two structs list the
-header's fields in the header's order, and the driver keeps the reference's
-function names and lambda lists (src/cuda-dit.lisp:52, 99, 137)."""
+header's fields in the header's order, and the drivers keep the reference's
+function names and lambda lists (src/cuda-dit.lisp:52, 99, 137; src/cuda-vae.lisp:15, 29, 94)."""
 import os
 import re
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LISP = os.path.join(ROOT, "lisp", "b200-dit.lisp")
+LISP_VAE = os.path.join(ROOT, "lisp", "b200-vae.lisp")
 HEADER = os.path.join(ROOT, "include", "exn_b200.h")
 
 
@@ -83,8 +84,8 @@ def header_struct(name):
     return fields
 
 
-def forms():
-    return read_forms(open(LISP).read())
+def forms(path=LISP):
+    return read_forms(open(path).read())
 
 
 # --------------------------------------------------------------------------- tests
@@ -97,8 +98,8 @@ def test_the_file_reads():
 
 def test_alien_routines_match_the_header():
     decl = header_functions()
-    routines = [f for f in forms() if f[0] == "sb-alien:define-alien-routine"]
-    assert len(routines) >= 8
+    routines = [f for path in (LISP, LISP_VAE) for f in forms(path) if f[0] == "sb-alien:define-alien-routine"]
+    assert len(routines) >= 14
     for f in routines:
         cname = f[1][0].strip('"')
         assert cname in decl, cname
@@ -110,7 +111,8 @@ def test_alien_routines_match_the_header():
             assert lisp_kind(t) == k, (cname, argname, t, k)
     bound = {f[1][0].strip('"') for f in routines}
     for needed in ("exn_open", "exn_close", "exn_last_error", "exn_load_gguf", "exn_velocity", "exn_generate",
-                   "exn_release", "exn_default_config"):
+                   "exn_release", "exn_default_config", "exn_vae_open", "exn_vae_close", "exn_vae_last_error",
+                   "exn_vae_load_safetensors", "exn_vae_decode", "exn_vae_release"):
         assert needed in bound, needed
 
 
@@ -131,3 +133,13 @@ def test_driver_keeps_the_reference_lambda_lists():
                                       ["prefix-key", "nil"], "ref"]
     assert defuns["dit-release"] == ["d"]
     assert "dit-euler" in defuns
+
+
+def test_vae_driver_keeps_the_reference_lambda_lists():
+    fs = forms(LISP_VAE)
+    assert fs[0] == ["in-package", "#:ex-nihilo"]
+    defuns = {f[1]: f[2] for f in fs if f[0] == "defun"}
+    # src/cuda-vae.lisp:15, 94, 29
+    assert defuns["upload-vae"] == ["path", "&key", ["device", "0"]]
+    assert defuns["vae-decode"] == ["v", "latent", "h", "w"]
+    assert defuns["vae-release"] == ["v"]

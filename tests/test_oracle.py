@@ -111,3 +111,18 @@ def test_mask_cases():
 def test_synth_generator_stats():
     u = O.synth_normal(1, 7, (1 << 16,), 1.0)
     assert abs(float(u.mean())) < 0.02 and abs(float(u.std()) - 1.0) < 0.02
+
+
+def test_vae_oracle_matches_ref_vae_golden(golden_dir):
+    """oracle/vae_oracle.py against the reference's own inspect/ref_vae.py (tests/golden/vae_small.npz:
+    the oracle's synthetic decoder written as a BF16 safetensors file, an 8 x 8 latent, 128 x 128
+    RGBA out): the same fp32 arithmetic, so rel-L2 < 1e-5."""
+    import hashlib
+    from oracle import vae_oracle as V
+    g = np.load(os.path.join(golden_dir, "vae_small.npz"))
+    sw = V.SynthVae(1)
+    z = O.synth_normal(0, 3000, (64, 8, 8))
+    assert hashlib.sha256(z.tobytes()).hexdigest() == str(g["latent_sha256"])
+    out = V.decode(sw, z)
+    assert out.shape == (4, 128, 128)
+    assert O.rel_l2(out, g["rgba"]) < 1e-5
