@@ -126,3 +126,33 @@ def test_vae_oracle_matches_ref_vae_golden(golden_dir):
     out = V.decode(sw, z)
     assert out.shape == (4, 128, 128)
     assert O.rel_l2(out, g["rgba"]) < 1e-5
+
+
+@pytest.mark.parametrize("case", ["text", "edit"])
+def test_encoder_oracle_matches_transformers_golden(golden_dir, case):
+    """oracle/encoder_oracle.py against transformers' Qwen3VLTextModel (tests/golden/encoder_small.npz,
+    made by make_encoder_golden.py with the oracle's synthetic weights): the last block's output before
+    the final norm, for text positions and an edit prompt's M-RoPE positions; fp32 both, rel-L2 < 1e-5."""
+    from oracle import encoder_oracle as EO
+    g = np.load(os.path.join(golden_dir, "encoder_small.npz"))
+    wt = EO.SynthEncoder(EO.SMALL, seed=1)
+    ids = g[case + "_ids"]
+    assert np.array_equal(ids, EO.synth_ids(EO.SMALL, len(ids), seed={"text": 0, "edit": 1}[case]))
+    pos = g[case + "_positions"]
+    want = EO.text_positions(len(ids)) if case == "text" else EO.edit_positions(6, 3, 5, 9)
+    assert np.array_equal(pos, want)
+    got = EO.states(wt, EO.SMALL, ids, pos)
+    assert O.rel_l2(got, g[case + "_states"]) < 1e-5
+
+
+def test_encoder_mrope_rule():
+    """mrope-table (src/encoder.lisp:26-39): frequency j turns by h where j mod 3 is 1 and by w where it
+    is 2, below 60; by t elsewhere.  For (i, i, i) it is plain RoPE at position i."""
+    from oracle import encoder_oracle as EO
+    a = EO.mrope_angles(EO.SMALL, np.array([[7, 100, 1000]]))[0]
+    inv = 5e6 ** (-(2.0 * np.arange(64)) / 128)
+    for j in range(64):
+        want = (1000 if j % 3 == 2 else 100 if j % 3 == 1 else 7) if j < 60 else 7
+        assert a[j] == want * inv[j]
+    t = EO.mrope_angles(EO.SMALL, EO.text_positions(5))
+    assert np.allclose(t, np.arange(5)[:, None] * inv[None, :], rtol=0, atol=0)
