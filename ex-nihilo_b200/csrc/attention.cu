@@ -82,8 +82,8 @@ struct Bars {
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int nq, int q0, int p, int l,
-                int b0, int b1, int width, float scale_log2, int qpairs, int heads, int n_pairs, const SpOut spo,
-                int* status) {
+                int b0, int b1, int width, float scale_log2, int qpairs, int heads, int kv_group, int n_pairs,
+                const SpOut spo, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tma_prefetch(&tmK);
       tma_prefetch(&tmV);
       griddep_wait();  // Q, K and V are the previous kernel's output
-      const int hx = head * 128;
+      const int hx = head * 128, kx = (head / kv_group) * 128;  // this head's Q columns, its K/V head's
       mbar_arrive_expect_tx(&bars->q_full, tiles * TILE_BYTES);
       for (int x = 0; x < tiles; ++x)
         for (int hf = 0; hf < 2; ++hf)
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         mbar_arrive_expect_tx(&bars->slot_full[slot], TILE_BYTES);
         const CUtensorMap* map = (t & 1) ? &tmV : &tmK;
         for (int hf = 0; hf < 2; ++hf)
-          tma_load_3d(smem + OFF_SLOT + slot * TILE_BYTES + hf * HALF, map, &bars->slot_full[slot], hx + hf * 64,
+          tma_load_3d(smem + OFF_SLOT + slot * TILE_BYTES + hf * HALF, map, &bars->slot_full[slot], kx + hf * 64,
                       (t >> 1) * TILE, sample);
         issued = t + 1;
       }
@@ -398,13 +398,16 @@ int attention_prepare() {
 int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   if (a.nq <= 0 || a.l <= 0 || a.width % 128 || a.heads * 128 != a.width || a.kv_rows < a.l) return -1;
   if (a.q0 + a.nq > a.l) return -1;
+  const int kv_heads = a.kv_heads > 0 ? a.kv_heads : a.heads;
+  if (a.heads % kv_heads) return -1;
+  const int kvw = kv_heads * 128;
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, TILE, 1};
   const uint64_t dq[3] = {static_cast<uint64_t>(a.width), static_cast<uint64_t>(a.nq),
                           static_cast<uint64_t>(a.batch)};
   const uint64_t sq[2] = {static_cast<uint64_t>(a.width) * 2, static_cast<uint64_t>(a.nq) * a.width * 2};
-  const uint64_t dk[3] = {static_cast<uint64_t>(a.width), static_cast<uint64_t>(a.l), static_cast<uint64_t>(a.batch)};
-  const uint64_t sk[2] = {static_cast<uint64_t>(a.width) * 2, static_cast<uint64_t>(a.kv_rows) * a.width * 2};
+  const uint64_t dk[3] = {static_cast<uint64_t>(kvw), static_cast<uint64_t>(a.l), static_cast<uint64_t>(a.batch)};
+  const uint64_t sk[2] = {static_cast<uint64_t>(kvw) * 2, static_cast<uint64_t>(a.kv_rows) * kvw * 2};
   if (make_tmap_bf16(&tq, a.q, 3, dq, sq, box) || make_tmap_bf16(&tk, a.k, 3, dk, sk, box) ||
       make_tmap_bf16(&tv, a.v, 3, dk, sk, box))
     return -4;
@@ -430,8 +433,8 @@ int attention_launch(const AttnArgs& a, int* d_status, cudaStream_t st) {
   spo.img0 = a.sp_img0;
   if (spo.out[0] != nullptr && (a.batch != 1 || spo.nl <= 0 || (spo.img0 > 0 && spo.pl <= 0))) return -1;
   return static_cast<int>(launch_pdl(k_attention, grid, dim3(ATT_THREADS), ATT_SMEM, st, tq, tk, tv, a.out, a.nq, a.q0,
-                                     a.p, a.l, a.b0, a.b1, a.width, a.scale_log2, qpairs, a.heads, n_pairs, spo,
-                                     d_status));
+                                     a.p, a.l, a.b0, a.b1, a.width, a.scale_log2, qpairs, a.heads, a.heads / kv_heads,
+                                     n_pairs, spo, d_status));
 }
 
 }  // namespace exn

@@ -65,6 +65,10 @@ struct GemmEpi {
   bf16* k = nullptr;
   bf16* v = nullptr;
   long long kv_sample_stride = 0;  // elements from one sample's K (V) rows to the next
+  // grouped K/V (the prompt encoder): columns [0, width) are q, then kv_width of k and of v, each
+  // stored with row stride kv_width (0: kv_width = width)
+  int kv_width = 0;
+  int rope_halves = 0;             // 0: dims (2j, 2j+1) turn by angle j; 1: dims (j, j+64)
   // EPI_QKV, sequence-parallel (group_w > 0): the tile's columns belong to head group
   // g = column / group_w, kept by rank g; each row is stored straight into rank g's buffers
   // (peer memory over NVLink): q at sp_q[g] + qrow * group_w, k and v at sp_k[g] / sp_v[g] +
@@ -101,11 +105,12 @@ int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st);
 
 struct AttnArgs {
   const bf16* q = nullptr;   // [B][nq][width]
-  const bf16* k = nullptr;   // [B][kv_rows][width]: this layer's keys
+  const bf16* k = nullptr;   // [B][kv_rows][kv_heads * 128]: this layer's keys
   const bf16* v = nullptr;
   bf16* out = nullptr;       // [B][nq][width]
   int batch = 1, nq = 0, q0 = 0, p = 0, l = 0, b0 = 0, b1 = 0;
   int heads = 0, width = 0;
+  int kv_heads = 0;          // K/V heads (0: heads); query head i reads K/V head i / (heads / kv_heads)
   int kv_rows = 0;           // row capacity of one sample's K/V
   float scale_log2 = 0.f;    // log2(e) / sqrt(128)
   // work split: CTAs of two query tiles, except (split_mode 2) a last round that would fill at most
@@ -193,6 +198,15 @@ void vae_softmax_launch(const float* s, bf16* p, int n, float scale, cudaStream_
 void vae_transpose_launch(const bf16* in, long long ld_in, bf16* out, int n, int c, cudaStream_t st);
 // a conv weight [o][i][taps] (f32) -> bf16 [rows][taps][cp], rows >= o and channels >= i zero
 void vae_weight_launch(const float* w, bf16* out, int o, int i, int taps, int rows, int cp, cudaStream_t st);
+
+// --- the prompt encoder's memory-bound kernels (encoder.cu) ---
+// x f32 [n][width] = table f32 [vocab][width] at rows ids[0..n)
+void enc_embed_launch(const float* table, const int* ids, float* x, int n, int width, cudaStream_t st);
+// table [n][64] (cos, sin): Qwen3-VL's interleaved M-RoPE of positions pos [n][3] (t, h, w)
+void enc_rope_launch(const int* pos, float2* table, int n, double theta, cudaStream_t st);
+// Q8_0 to f32, exactly: from split (qs, d) or from GGUF's 34-byte blocks
+void q8_to_f32_launch(const int8_t* qs, const __half* d, float* out, long long n, cudaStream_t st);
+void q8_raw_to_f32_launch(const uint8_t* raw, float* out, long long n, cudaStream_t st);
 
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.

@@ -509,6 +509,10 @@ int gemm_i8_launch(const GemmArgs& g, const int8_t* a, const int8_t* b, int* d_s
 
 int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK) return -1;
+  if (g.epi == EPI_QKV) {  // whole heads a tile: q, k and v widths multiples of 256, N their sum
+    const int kvw = g.ep.kv_width > 0 ? g.ep.kv_width : g.ep.width;
+    if (g.ep.width <= 0 || g.ep.width % 256 || kvw % 256 || g.N != g.ep.width + 2 * kvw) return -1;
+  }
   if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b)) & 15) return -1;
   if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return -1;
   if (g.pairs && g.N % 256 == 0 && num_sms >= 2) {

@@ -149,8 +149,9 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
     }
   } else if constexpr (EPI == EPI_QKV) {
     static_assert(BN == 256, "QKV tiles hold two whole heads");
-    const int sec = col0 / e.width;            // 0 q, 1 k, 2 v
-    const int hc0 = col0 - sec * e.width;      // first column within q / k / v
+    const int kvw = e.kv_width > 0 ? e.kv_width : e.width;
+    const int sec = col0 < e.width ? 0 : 1 + (col0 - e.width) / kvw;        // 0 q, 1 k, 2 v
+    const int hc0 = sec == 0 ? col0 : col0 - e.width - (sec - 1) * kvw;     // first column within q / k / v
     const int t = row % e.seg_in, b = row / e.seg_in;
     bf16* dst;
     if (e.group_w > 0) {  // sequence-parallel: straight into the rank that keeps this head group
@@ -167,7 +168,7 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
     } else if (sec == 0)
       dst = e.q + static_cast<long long>(row) * e.width + hc0;
     else
-      dst = (sec == 1 ? e.k : e.v) + b * e.kv_sample_stride + static_cast<long long>(e.n0 + t) * e.width + hc0;
+      dst = (sec == 1 ? e.k : e.v) + b * e.kv_sample_stride + static_cast<long long>(e.n0 + t) * kvw + hc0;
     const float* nw = sec == 0 ? e.norm_q : e.norm_k;
     const float2* cs = e.rope + static_cast<long long>(e.n0 + t) * 64;
 #pragma unroll 1
@@ -186,13 +187,24 @@ __device__ __forceinline__ void epilogue(uint32_t taddr, int row, bool valid, in
 #pragma unroll
         for (int i = 0; i < 128; ++i) ss += v[i] * v[i];
         const float inv = rsqrtf(ss / 128.f + 1e-6f);
+        if (e.rope_halves) {  // dims j and j + 64 turn together (rotate-half form)
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float a = v[2 * j] * inv * __ldg(nw + 2 * j);
-          const float bq = v[2 * j + 1] * inv * __ldg(nw + 2 * j + 1);
-          const float2 r = __ldg(cs + j);
-          v[2 * j] = a * r.x - bq * r.y;
-          v[2 * j + 1] = a * r.y + bq * r.x;
+          for (int j = 0; j < 64; ++j) {
+            const float a = v[j] * inv * __ldg(nw + j);
+            const float bq = v[j + 64] * inv * __ldg(nw + j + 64);
+            const float2 r = __ldg(cs + j);
+            v[j] = a * r.x - bq * r.y;
+            v[j + 64] = a * r.y + bq * r.x;
+          }
+        } else {              // dims 2j and 2j + 1 turn together (complex-pair form)
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float a = v[2 * j] * inv * __ldg(nw + 2 * j);
+            const float bq = v[2 * j + 1] * inv * __ldg(nw + 2 * j + 1);
+            const float2 r = __ldg(cs + j);
+            v[2 * j] = a * r.x - bq * r.y;
+            v[2 * j + 1] = a * r.y + bq * r.x;
+          }
         }
       }
 #pragma unroll

@@ -48,6 +48,11 @@ class Config(ctypes.Structure):
                 ("device", ctypes.c_int)]
 
 
+class EncConfig(ctypes.Structure):
+    _fields_ = [("width", ctypes.c_int), ("layers", ctypes.c_int), ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("theta", ctypes.c_double), ("device", ctypes.c_int)]
+
+
 class Ref(ctypes.Structure):
     _fields_ = [("a", ctypes.c_int), ("latent", ctypes.POINTER(ctypes.c_float)), ("rh", ctypes.c_int),
                 ("rw", ctypes.c_int)]
@@ -98,6 +103,18 @@ def lib():
         "exn_vae_decode": (ctypes.c_int, [H, fp, ctypes.c_int, ctypes.c_int, fp]),
         "exn_vae_release": (ctypes.c_int, [H]),
         "exn_test_vae_last_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
+        "exn_enc_default_config": (None, [ctypes.POINTER(EncConfig)]),
+        "exn_enc_open": (ctypes.c_int, [ctypes.POINTER(EncConfig), ctypes.POINTER(H)]),
+        "exn_enc_close": (None, [H]),
+        "exn_enc_last_error": (ctypes.c_char_p, [H]),
+        "exn_enc_load_gguf": (ctypes.c_int, [H, ctypes.c_char_p]),
+        "exn_enc_load_synthetic": (ctypes.c_int, [H, ctypes.c_uint64]),
+        "exn_enc_weights_ready": (ctypes.c_int, [H]),
+        "exn_enc_states": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_int32), fp]),
+        "exn_enc_release": (ctypes.c_int, [H]),
+        "exn_test_enc_last_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
+        "exn_test_enc_weights_digest": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_uint64)]),
         "exn_release": (ctypes.c_int, [H]),
         "exn_comm_unique_id": (ctypes.c_int, [vp]),
         "exn_comm_init": (ctypes.c_int, [H, vp, ctypes.c_int, ctypes.c_int]),
@@ -370,6 +387,81 @@ class Vae:
         return ms.value
 
 
+class Encoder:
+    """The prompt encoder (Qwen3-VL-8B's text model) on one CUDA device: what load-encoder returns
+    (src/encoder.lisp:41-48).  SHAPE overrides fields of exn_enc_default_config (width, layers,
+    heads, kv_heads, ffn, vocab, theta)."""
+
+    def __init__(self, device=0, **shape):
+        cfg = EncConfig()
+        lib().exn_enc_default_config(ctypes.byref(cfg))
+        for k, v in shape.items():
+            setattr(cfg, k, v)
+        cfg.device = device
+        h = ctypes.c_void_p()
+        rc = lib().exn_enc_open(ctypes.byref(cfg), ctypes.byref(h))
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_enc_last_error(None).decode(errors="replace"))
+        self.h = h
+        self.cfg = cfg
+
+    def _ck(self, rc):
+        if rc != EXN_OK:
+            raise ExnError(rc, lib().exn_enc_last_error(self.h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().exn_enc_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def load_gguf(self, path):
+        self._ck(lib().exn_enc_load_gguf(self.h, str(path).encode()))
+
+    def load_synthetic(self, seed=1):
+        self._ck(lib().exn_enc_load_synthetic(self.h, seed))
+
+    def states(self, ids, positions=None):
+        """encoder-states: (n, width) float32, the last block's output before the final norm.
+        POSITIONS: (n, 3) ints (t, h, w) or None for a text prompt's (i, i, i)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        n = len(ids)
+        pos = None
+        if positions is not None:
+            pos = np.ascontiguousarray(positions, dtype=np.int32)
+            if pos.shape != (n, 3):
+                raise ExnError(1, "positions must be (n, 3), got %s" % (pos.shape,))
+        out = np.empty((n, self.cfg.width), dtype=np.float32)
+        ip = ctypes.POINTER(ctypes.c_int32)
+        self._ck(lib().exn_enc_states(self.h, ids.ctypes.data_as(ip), n,
+                                      pos.ctypes.data_as(ip) if pos is not None else None, _fp(out)))
+        return out
+
+    def release(self):
+        self._ck(lib().exn_enc_release(self.h))
+
+    def last_ms(self):
+        ms = ctypes.c_double()
+        self._ck(lib().exn_test_enc_last_ms(self.h, ctypes.byref(ms)))
+        return ms.value
+
+    def weights_digest(self):
+        d = ctypes.c_uint64()
+        self._ck(lib().exn_test_enc_weights_digest(self.h, ctypes.byref(d)))
+        return d.value
+
+
 # ---- the reference's names
 
 def upload_dit(path, device=0, **shape) -> Dit:
@@ -417,3 +509,19 @@ def vae_decode(v: Vae, latent, h, w):
 def vae_release(v: Vae):
     """(vae-release v), src/cuda-vae.lisp:29-33."""
     v.release()
+
+
+def load_encoder(path, device=0, **shape) -> Encoder:
+    """(load-encoder path :device device), src/encoder.lisp:41-48, on the B200."""
+    e = Encoder(device=device, **shape)
+    try:
+        e.load_gguf(path)
+    except Exception:
+        e.close()
+        raise
+    return e
+
+
+def encoder_states(e: Encoder, ids, positions=None):
+    """(encoder-states model ids :rope (mrope-table positions ...)), src/encoder.lisp:143-183."""
+    return e.states(ids, positions)

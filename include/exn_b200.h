@@ -187,6 +187,55 @@ int exn_vae_decode(exn_vae* v, const float* latent, int h, int w, float* rgba);
 /* vae-release: the decoder's scratch freed (the weights stay). */
 int exn_vae_release(exn_vae* v);
 
+/* ---- The prompt encoder: Qwen3-VL-8B's text model on the same GPU as the DiT, token ids to the
+ * states the DiT reads.  Each entry point replaces one function of src/encoder.lisp:
+ *
+ *   exn_enc_open + exn_enc_load_gguf
+ *                      (load-encoder path :device d)      src/encoder.lisp:41-48 (the qwen3vl GGUF)
+ *   exn_enc_states     (encoder-states model ids :rope r)  src/encoder.lisp:143-183
+ *   exn_enc_release    (free-context ctx)                  src/encoder.lisp:180
+ *
+ * Tokenising (il::tokenize) and cutting the system turn's rows (encode-prompt,
+ * src/encoder.lisp:55-67) stay with the caller.  Matrices run on the tensor cores with bf16
+ * operands and fp32 accumulation; the residual stream and the embedding rows are fp32. */
+typedef struct exn_enc exn_enc;
+
+typedef struct exn_enc_config {
+  int width;     /* 4096 */
+  int layers;    /* 36 */
+  int heads;     /* 32 query heads of 128 */
+  int kv_heads;  /* 8 key/value heads of 128 */
+  int ffn;       /* 12288 */
+  int vocab;     /* 151936 */
+  double theta;  /* 5e6, the M-RoPE base */
+  int device;
+} exn_enc_config;
+
+void exn_enc_default_config(exn_enc_config* cfg);
+int exn_enc_open(const exn_enc_config* cfg, exn_enc** out);
+void exn_enc_close(exn_enc* e);
+const char* exn_enc_last_error(const exn_enc* e);
+
+/* The text model's tensors from a qwen3vl (or qwen3) GGUF, llama.cpp's names (token_embd,
+ * blk.N.attn_q / attn_k / attn_v / attn_output / attn_q_norm / attn_k_norm / attn_norm /
+ * ffn_gate / ffn_up / ffn_down / ffn_norm); each checked against the configuration's dims; Q8_0,
+ * BF16, F16 or F32.  The final norm and the LM head are not read. */
+int exn_enc_load_gguf(exn_enc* e, const char* path);
+
+/* Every tensor from the deterministic synthetic generator (matrices N(0, std) as Q8_0, vectors
+ * 1 + N(0, std)), the same bits as the test oracle's. */
+int exn_enc_load_synthetic(exn_enc* e, uint64_t seed);
+int exn_enc_weights_ready(const exn_enc* e);
+
+/* encoder-states: every token's state after the last block, before the final norm.  IDS: N token
+ * ids (0 <= id < vocab).  POSITIONS: N x 3 ints (t, h, w) per token, Qwen3-VL's interleaved M-RoPE
+ * as src/encoder.lisp:26-39 builds it, or NULL for a text prompt's (i, i, i).  STATES: N x width
+ * floats, row-major. */
+int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, float* states);
+
+/* The encoder's scratch freed (the weights stay). */
+int exn_enc_release(exn_enc* e);
+
 #ifdef __cplusplus
 }
 #endif

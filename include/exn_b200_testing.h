@@ -136,6 +136,14 @@ int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, doubl
  * latent's upload to the start of the pixels' download. */
 int exn_test_vae_last_ms(const exn_vae* v, double* ms);
 
+/* Device time in ms (CUDA events on the encoder's stream) of the last exn_enc_states, from the ids'
+ * upload to the states' download. */
+int exn_test_enc_last_ms(const exn_enc* e, double* ms);
+
+/* An order-independent digest of every byte of the encoder's weights on the device (the bf16
+ * matrices, the fp32 vectors and embedding table), to compare two loads. */
+int exn_test_enc_weights_digest(exn_enc* e, uint64_t* out);
+
 #ifdef __cplusplus
 }
 #endif

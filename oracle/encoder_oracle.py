@@ -14,7 +14,7 @@ not in the reference tree; its qwen3 forward is the published Qwen3 architecture
                 x += softmax_causal(q k^T / sqrt(128)) v  Wo^T      (query head i reads kv head i / 4)
                 h = rms(x) * ffn_norm;  x += (silu(h Wg^T) * (h Wu^T)) Wd^T
 
-Parity is pinned by tests/golden/make_golden.py, which loads this module's synthetic weights into
+Parity is pinned by tests/golden/make_encoder_golden.py, which loads this module's synthetic weights into
 transformers' own ``Qwen3VLTextModel`` (fp32, eager attention) and stores the last block's output
 for text positions and for an edit prompt's M-RoPE positions; tests/test_oracle.py holds this
 module to it.
@@ -185,3 +185,39 @@ def states(wt, sh: EncShape, ids, positions=None, layers=None):
     for i in range(sh.layers if layers is None else layers):
         x = block(wt, sh, i, x, cos, sin)
     return x
+
+
+def write_gguf(path, wt: SynthEncoder, arch="qwen3vl", matrix_type="q8_0", drop=(), extra=(), bad_dims=None):
+    """The synthetic encoder as a GGUF with gguf-py, llama.cpp's tensor names.  MATRIX_TYPE 'q8_0'
+    (the quantised values), 'bf16' or 'f32' (the dequantised ones); the embedding table goes the
+    same way.  DROP / EXTRA / BAD_DIMS plant the faults the loader must name (on the CPU)."""
+    import gguf
+    wr = gguf.GGUFWriter(str(path), arch=arch)
+    for name, dims in encoder_tensors(wt.shape):
+        if name in drop:
+            continue
+        if len(dims) == 1:
+            wr.add_tensor(name, wt(name))
+            continue
+        qs, d = wt.q8(name)
+        rows, cols = qs.shape
+        if bad_dims == name:
+            wr.add_tensor(name, np.ascontiguousarray(D.q8_0_dequantize(qs, d)[:, : cols - 32]))
+        elif matrix_type == "q8_0":
+            wr.add_tensor(name, D.q8_0_pack(qs, d).reshape(rows, cols // 32 * 34),
+                          raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        elif matrix_type == "f32":
+            wr.add_tensor(name, D.q8_0_dequantize(qs, d))
+        elif matrix_type == "bf16":
+            v = D.q8_0_dequantize(qs, d)
+            u = v.view(np.uint32)
+            bits = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+            wr.add_tensor(name, bits.astype(np.uint16), raw_dtype=gguf.GGMLQuantizationType.BF16)
+        else:
+            raise ValueError(matrix_type)
+    for name in extra:
+        wr.add_tensor(name, np.ones(wt.shape.width, dtype=np.float32))
+    wr.write_header_to_file()
+    wr.write_kv_data_to_file()
+    wr.write_tensors_to_file()
+    wr.close()

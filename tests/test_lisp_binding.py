@@ -1,17 +1,19 @@
-"""The Lisp bindings (lisp/b200-dit.lisp, lisp/b200-vae.lisp) against the C header they bind.
+"""The Lisp bindings (lisp/b200-dit.lisp, b200-vae.lisp, b200-encoder.lisp) against the C header they bind.
 
 SBCL is not installed here, so the binding cannot run; these checks read it as
 text: the file is balanced s-expressions, every sb-alien routine names a
 function that include/exn_b200.h declares, with the same number of arguments
 and the same kind of each argument and result, the two structs list the
 header's fields in the header's order, and the drivers keep the reference's
-function names and lambda lists (src/cuda-dit.lisp:52, 99, 137; src/cuda-vae.lisp:15, 29, 94)."""
+function names and lambda lists (src/cuda-dit.lisp:52, 99, 137; src/cuda-vae.lisp:15, 29, 94;
+src/encoder.lisp:26, 41, 143)."""
 import os
 import re
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LISP = os.path.join(ROOT, "lisp", "b200-dit.lisp")
 LISP_VAE = os.path.join(ROOT, "lisp", "b200-vae.lisp")
+LISP_ENC = os.path.join(ROOT, "lisp", "b200-encoder.lisp")
 HEADER = os.path.join(ROOT, "include", "exn_b200.h")
 
 
@@ -98,8 +100,9 @@ def test_the_file_reads():
 
 def test_alien_routines_match_the_header():
     decl = header_functions()
-    routines = [f for path in (LISP, LISP_VAE) for f in forms(path) if f[0] == "sb-alien:define-alien-routine"]
-    assert len(routines) >= 14
+    routines = [f for path in (LISP, LISP_VAE, LISP_ENC) for f in forms(path)
+                if f[0] == "sb-alien:define-alien-routine"]
+    assert len(routines) >= 21
     for f in routines:
         cname = f[1][0].strip('"')
         assert cname in decl, cname
@@ -112,17 +115,20 @@ def test_alien_routines_match_the_header():
     bound = {f[1][0].strip('"') for f in routines}
     for needed in ("exn_open", "exn_close", "exn_last_error", "exn_load_gguf", "exn_velocity", "exn_generate",
                    "exn_release", "exn_default_config", "exn_vae_open", "exn_vae_close", "exn_vae_last_error",
-                   "exn_vae_load_safetensors", "exn_vae_decode", "exn_vae_release"):
+                   "exn_vae_load_safetensors", "exn_vae_decode", "exn_vae_release", "exn_enc_default_config",
+                   "exn_enc_open", "exn_enc_close", "exn_enc_last_error", "exn_enc_load_gguf", "exn_enc_states",
+                   "exn_enc_release"):
         assert needed in bound, needed
 
 
 def test_structs_match_the_header():
     types = {}
-    for f in forms():
+    for f in forms() + forms(LISP_ENC):
         if f[0] == "sb-alien:define-alien-type" and isinstance(f[2], list) and f[2][0] == "sb-alien:struct":
             types[f[2][1]] = [(fld[0], lisp_kind(fld[1])) for fld in f[2][2:]]
     assert types["exn-config"] == header_struct("exn_config")
     assert types["exn-ref"] == header_struct("exn_ref")
+    assert types["exn-enc-config"] == header_struct("exn_enc_config")
 
 
 def test_driver_keeps_the_reference_lambda_lists():
@@ -143,3 +149,14 @@ def test_vae_driver_keeps_the_reference_lambda_lists():
     assert defuns["upload-vae"] == ["path", "&key", ["device", "0"]]
     assert defuns["vae-decode"] == ["v", "latent", "h", "w"]
     assert defuns["vae-release"] == ["v"]
+
+
+def test_encoder_driver_keeps_the_reference_lambda_lists():
+    fs = forms(LISP_ENC)
+    assert fs[0] == ["in-package", "#:ex-nihilo"]
+    defuns = {f[1]: f[2] for f in fs if f[0] == "defun"}
+    # src/encoder.lisp:41, 143, 26, 50
+    assert defuns["load-encoder"] == ["path", "&key", "device", "threads"]
+    assert defuns["encoder-states"] == ["model", "ids", "&key", "rope"]
+    assert defuns["mrope-table"] == ["positions", "rd", "base"]
+    assert defuns["encoder-gpu-p"] == ["model"]
