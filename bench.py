@@ -107,6 +107,14 @@ def vae_flops(h=H, w=WW):
     return f + 18.0 * 144 * 4 * n
 
 
+ENC_PROMPT = 141   # config 2's 128 prompt rows plus the chat template's system turn (about 13 tokens)
+
+
+def encoder_weight_bytes(width=4096, layers=36, q=4096, kv=1024, ffn=12288):
+    """Bytes of the prompt encoder's bf16 matrices, read once a prompt (Qwen3-VL-8B's text model)."""
+    return 2.0 * layers * width * (q + 2 * kv + q + 3 * ffn)
+
+
 def peak_clock_mhz():
     """The median SM clock under load while MEASURED_PEAKS.json's sustained peak was measured."""
     try:
@@ -466,6 +474,31 @@ def run_exn(args):
                              "finite": bool(np.isfinite(rgba).all()),
                              "timing": "CUDA events on the decoder's stream, latent upload to pixel download, best "
                                        "of 3 after 2 warm-up decodes; synthetic bf16 weights"}
+    # the step before the DiT: the prompt encoder on one prompt (rank 0, 1 GPU lines only)
+    if world == 1 and not args.no_vae:
+        enc = E.Encoder(device=local)
+        enc.load_synthetic(1)
+        ids = (np.arange(ENC_PROMPT, dtype=np.int64) * 7919 % 151936).astype(np.int32)
+        for _ in range(2):
+            enc.states(ids)
+        em = []
+        for _ in range(5):
+            st_ = enc.states(ids)
+            em.append(enc.last_ms())
+        enc.close()
+        wb = encoder_weight_bytes()
+        ef = 2.0 * ENC_PROMPT * wb / 2
+        out["prompt_encoder"] = {"workload": "prompt encoder (Qwen3-VL-8B text model, 36 blocks): %d tokens "
+                                             "(config 2's prompt with the template's system turn)" % ENC_PROMPT,
+                                 "ms": round(min(em), 3), "tokens_per_s": round(ENC_PROMPT / (min(em) * 1e-3), 1),
+                                 "weight_gb": round(wb / 1e9, 3),
+                                 "hbm_gbs": round(wb / (min(em) * 1e-3) / 1e9, 1),
+                                 "hbm_frac": round(wb / (min(em) * 1e-3) / 1e9 / hbm, 4),
+                                 "tflops": round(ef / (min(em) * 1e-3) / 1e12, 1),
+                                 "finite": bool(np.isfinite(st_).all()),
+                                 "timing": "CUDA events on the encoder's stream, ids upload to states download, "
+                                           "best of 5 after 2 warm-up passes; synthetic weights (Q8_0 values "
+                                           "held as bf16); bound: its bf16 weights read once"}
     if world == 1 and not args.no_cpu:
         with all_host_threads():
             bs = cpu_block_seconds()
@@ -607,7 +640,8 @@ def main():
                     help="cfg2: one picture per GPU per step (default); cfg4: one 8704-row edit over all GPUs; "
                          "cfg5: 64 pictures split over the GPUs")
     ap.add_argument("--pictures", type=int, default=64, help="cfg5: pictures in the job")
-    ap.add_argument("--no-vae", action="store_true", help="skip the VAE decoder timing (1 GPU lines)")
+    ap.add_argument("--no-vae", action="store_true",
+                    help="skip the VAE decoder and prompt encoder timings (1 GPU lines)")
     ap.add_argument("--no-sp-edit", action="store_true",
                     help="N > 1: skip the config-4 edit shared by all GPUs that follows the replica timing")
     args = ap.parse_args()
