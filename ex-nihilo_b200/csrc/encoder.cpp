@@ -38,6 +38,10 @@ thread_local std::string g_enc_open_error;
 constexpr uint32_t kStream0 = 30000;  // synthetic stream of tensor i: kStream0 + i
 constexpr int kHeadDim = 128;
 constexpr int kMaxTokens = 32768;
+// prompts of at most this many tokens run their GEMMs split along K (their tile grids cover a
+// fraction of the SMs), in at most kMaxSplits parts
+constexpr int kSplitRows = 512;
+constexpr int kMaxSplits = 8;
 
 struct Spec {
   std::string name;
@@ -229,7 +233,24 @@ struct Scratch {
   float2* rope;
   int* ids;
   int* pos;
+  float* part;  // split-K partials: [splits][n][N] for prompts of at most kSplitRows tokens
 };
+
+// the split of a GEMM with TILES 256 x 256 output tiles and NUM_KB k-blocks over CLUSTERS CTA
+// pairs: the count of parts (1 .. kMaxSplits) whose work items fill their last wave best
+int split_for(int tiles, int num_kb, int clusters) {
+  int best = 1;
+  double best_eff = 0;
+  for (int s = 1; s <= kMaxSplits && s <= num_kb; ++s) {
+    const double w = static_cast<double>(tiles) * s / clusters;
+    const double eff = w / std::ceil(w);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
 
 size_t scratch_bytes(const exn_enc_config& c, int n, Scratch* s, char* base) {
   const int q = q_width(c), kv = kv_width(c);
@@ -249,6 +270,9 @@ size_t scratch_bytes(const exn_enc_config& c, int n, Scratch* s, char* base) {
   t.rope = reinterpret_cast<float2*>(take(static_cast<size_t>(n) * 64 * 8));
   t.ids = reinterpret_cast<int*>(take(static_cast<size_t>(n) * 4));
   t.pos = reinterpret_cast<int*>(take(static_cast<size_t>(n) * 12));
+  const size_t widest = std::max({static_cast<size_t>(q + 2 * kv), static_cast<size_t>(2 * c.ffn),
+                                  static_cast<size_t>(c.width)});
+  t.part = reinterpret_cast<float*>(take(kMaxSplits * static_cast<size_t>(std::min(n, kSplitRows)) * widest * 4));
   if (s) *s = t;
   return off;
 }
@@ -272,14 +296,43 @@ int gemm(exn_enc* e, const GemmArgs& g, const char* what, int layer) {
   return EXN_OK;
 }
 
-// one block of the text model over the N rows of S (x updated in place)
+// parts of a thin prompt's GEMM with N output columns and K deep (1: no split)
+int splits(const exn_enc* e, int n, int N, int K) {
+  if (n > kSplitRows) return 1;
+  return split_for(((n + 255) / 256) * (N / 256), K / 64, e->sms / 2);
+}
+
+// a split-K GEMM of A [n][K] and B [N][K] into the partials of S
+int gemm_split(exn_enc* e, const bf16* a, const bf16* b, int n, int N, int K, int parts, const Scratch& s,
+               const char* what, int layer) {
+  GemmArgs g;
+  g.a = a;
+  g.lda = K;
+  g.b = b;
+  g.ldb = K;
+  g.M = n;
+  g.N = N;
+  g.K = K;
+  g.epi = EPI_F32;
+  g.ep.out = s.part;
+  g.ep.ld_out = N;
+  g.ep.splits = parts;
+  return gemm(e, g, what, layer);
+}
+
+// one block of the text model over the N rows of S (x updated in place).  A thin prompt's GEMMs
+// run split along K into fp32 partials, summed (in split order) by the kernel that applies the
+// epilogue; a longer prompt's have the epilogue fused.
 int block(exn_enc* e, int li, int n, const Scratch& s) {
   const exn_enc_config& c = e->cfg;
   const EncLayer& L = e->layers[li];
   const int q = q_width(c), kv = kv_width(c);
-  int rc;
+  int rc, sp;
   rms_launch(s.x, L.attn_norm, s.xn, n, c.width, e->st);
-  {  // q, k, v: per-head RMS norm and RoPE on halves in the epilogue
+  if ((sp = splits(e, n, q + 2 * kv, c.width)) > 1) {
+    if ((rc = gemm_split(e, s.xn, L.qkv, n, q + 2 * kv, c.width, sp, s, "q/k/v", li))) return rc;
+    enc_qkv_sum_launch(s.part, sp, n, q, kv, L.q_norm, L.k_norm, s.rope, s.q, s.k, s.v, e->st);
+  } else {  // q, k, v: per-head RMS norm and RoPE on halves in the epilogue
     GemmArgs g;
     g.a = s.xn;
     g.lda = c.width;
@@ -320,7 +373,10 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
     const int r = attention_launch(a, e->d_status, e->st);
     if (r) return efail(e, EXN_ECUDA, "encoder block %d: attention (%d rows) launch failed: %d", li, n, r);
   }
-  {  // x += attn Wo^T
+  if ((sp = splits(e, n, c.width, q)) > 1) {
+    if ((rc = gemm_split(e, s.xn, L.o, n, c.width, q, sp, s, "attn_output", li))) return rc;
+    enc_resid_sum_launch(s.part, sp, n, c.width, s.x, e->st);
+  } else {  // x += attn Wo^T
     GemmArgs g;
     g.a = s.xn;
     g.lda = q;
@@ -336,7 +392,10 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
     if ((rc = gemm(e, g, "attn_output", li))) return rc;
   }
   rms_launch(s.x, L.ffn_norm, s.xn, n, c.width, e->st);
-  {  // h = silu(x Wg^T) * (x Wu^T)
+  if ((sp = splits(e, n, 2 * c.ffn, c.width)) > 1) {
+    if ((rc = gemm_split(e, s.xn, L.gu, n, 2 * c.ffn, c.width, sp, s, "ffn_gate/up", li))) return rc;
+    enc_swiglu_sum_launch(s.part, sp, n, c.ffn, s.h, e->st);
+  } else {  // h = silu(x Wg^T) * (x Wu^T)
     GemmArgs g;
     g.a = s.xn;
     g.lda = c.width;
@@ -350,7 +409,10 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
     g.ep.ld_out = c.ffn;
     if ((rc = gemm(e, g, "ffn_gate/up", li))) return rc;
   }
-  {  // x += h Wd^T
+  if ((sp = splits(e, n, c.width, c.ffn)) > 1) {
+    if ((rc = gemm_split(e, s.h, L.down, n, c.width, c.ffn, sp, s, "ffn_down", li))) return rc;
+    enc_resid_sum_launch(s.part, sp, n, c.width, s.x, e->st);
+  } else {  // x += h Wd^T
     GemmArgs g;
     g.a = s.h;
     g.lda = c.ffn;

@@ -49,6 +49,91 @@ __global__ void k_q8_raw_to_f32(const uint8_t* __restrict__ raw, float* __restri
   out[i] = static_cast<float>(static_cast<int8_t>(blk[2 + (i & 31)])) * __half2float(d);
 }
 
+// ---- the epilogues of a split-K GEMM: PART [splits][n][N] fp32 partials summed in split order
+
+// q / k / v: one warp a (row, head of 128 columns); q and k heads RMS-normed (eps 1e-6) times
+// their weight and turned by RoPE on halves (dims j and j + 64 by angle j of ROPE [row][64]);
+// lane l holds dims l, l + 32, l + 64, l + 96
+__global__ void k_enc_qkv_sum(const float* __restrict__ part, int splits, int n, int qw, int kvw,
+                              const float* __restrict__ norm_q, const float* __restrict__ norm_k,
+                              const float2* __restrict__ rope, bf16* __restrict__ q, bf16* __restrict__ k,
+                              bf16* __restrict__ v) {
+  const int heads = (qw + 2 * kvw) / 128;
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= static_cast<long long>(n) * heads) return;
+  const int r = static_cast<int>(wid / heads), h = static_cast<int>(wid - static_cast<long long>(r) * heads);
+  const int N = qw + 2 * kvw;
+  const long long stride = static_cast<long long>(n) * N;
+  const float* p = part + static_cast<long long>(r) * N + h * 128 + lane;
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = p[32 * i];
+  for (int sp = 1; sp < splits; ++sp)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] += p[sp * stride + 32 * i];
+  const int col = h * 128;
+  const int sec = col < qw ? 0 : (col < qw + kvw ? 1 : 2);
+  if (sec < 2) {
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / 128.f + 1e-6f);
+    const float* w = sec == 0 ? norm_q : norm_k;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = x[i] * inv * __ldg(w + lane + 32 * i);
+    const float2 c0 = __ldg(rope + static_cast<long long>(r) * 64 + lane);
+    const float2 c1 = __ldg(rope + static_cast<long long>(r) * 64 + lane + 32);
+    const float a0 = x[0], b0 = x[2], a1 = x[1], b1 = x[3];
+    x[0] = a0 * c0.x - b0 * c0.y;
+    x[2] = a0 * c0.y + b0 * c0.x;
+    x[1] = a1 * c1.x - b1 * c1.y;
+    x[3] = a1 * c1.y + b1 * c1.x;
+  }
+  bf16* dst = sec == 0 ? q + static_cast<long long>(r) * qw + col
+                       : (sec == 1 ? k + static_cast<long long>(r) * kvw + (col - qw)
+                                   : v + static_cast<long long>(r) * kvw + (col - qw - kvw));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
+}
+
+// x [n][w] += the sum of the partials
+__global__ void k_enc_resid_sum(const float* __restrict__ part, int splits, long long count, float* __restrict__ x) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= count / 4) return;
+  const float4* p = reinterpret_cast<const float4*>(part);
+  float4 a = p[i];
+  for (int sp = 1; sp < splits; ++sp) {
+    const float4 b = p[sp * (count / 4) + i];
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+  }
+  float4* xp = reinterpret_cast<float4*>(x) + i;
+  float4 o = *xp;
+  o.x += a.x;
+  o.y += a.y;
+  o.z += a.z;
+  o.w += a.w;
+  *xp = o;
+}
+
+// h [n][ffn] bf16 = silu(gate) * up, the partials' columns gate and up interleaved by 128
+__global__ void k_enc_swiglu_sum(const float* __restrict__ part, int splits, int n, int ffn, bf16* __restrict__ h) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(n) * ffn) return;
+  const int r = static_cast<int>(i / ffn), j = static_cast<int>(i - static_cast<long long>(r) * ffn);
+  const long long stride = static_cast<long long>(n) * 2 * ffn;
+  const float* p = part + static_cast<long long>(r) * 2 * ffn + (j >> 7) * 256 + (j & 127);
+  float g = p[0], u = p[128];
+  for (int sp = 1; sp < splits; ++sp) {
+    g += p[sp * stride];
+    u += p[sp * stride + 128];
+  }
+  h[i] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
+}
+
 unsigned blocks(long long n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
 }  // namespace
@@ -67,6 +152,21 @@ void q8_to_f32_launch(const int8_t* qs, const __half* d, float* out, long long n
 
 void q8_raw_to_f32_launch(const uint8_t* raw, float* out, long long n, cudaStream_t st) {
   k_q8_raw_to_f32<<<blocks(n, 256), 256, 0, st>>>(raw, out, n);
+}
+
+void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, const float* norm_q,
+                        const float* norm_k, const float2* rope, bf16* q, bf16* k, bf16* v, cudaStream_t st) {
+  const long long warps = static_cast<long long>(n) * ((qw + 2 * kvw) / 128);
+  k_enc_qkv_sum<<<blocks(warps * 32, 256), 256, 0, st>>>(part, splits, n, qw, kvw, norm_q, norm_k, rope, q, k, v);
+}
+
+void enc_resid_sum_launch(const float* part, int splits, int n, int w, float* x, cudaStream_t st) {
+  const long long count = static_cast<long long>(n) * w;
+  k_enc_resid_sum<<<blocks(count / 4, 256), 256, 0, st>>>(part, splits, count, x);
+}
+
+void enc_swiglu_sum_launch(const float* part, int splits, int n, int ffn, bf16* h, cudaStream_t st) {
+  k_enc_swiglu_sum<<<blocks(static_cast<long long>(n) * ffn, 256), 256, 0, st>>>(part, splits, n, ffn, h);
 }
 
 }  // namespace exn

@@ -69,6 +69,9 @@ struct GemmEpi {
   // stored with row stride kv_width (0: kv_width = width)
   int kv_width = 0;
   int rope_halves = 0;             // 0: dims (2j, 2j+1) turn by angle j; 1: dims (j, j+64)
+  // split-K (EPI_F32 on CTA pairs): part s of the k-blocks of every tile into output rows s * M ..,
+  // fp32 partials the caller sums (1: no split)
+  int splits = 1;
   // EPI_QKV, sequence-parallel (group_w > 0): the tile's columns belong to head group
   // g = column / group_w, kept by rank g; each row is stored straight into rank g's buffers
   // (peer memory over NVLink): q at sp_q[g] + qrow * group_w, k and v at sp_k[g] / sp_v[g] +
@@ -207,6 +210,12 @@ void enc_rope_launch(const int* pos, float2* table, int n, double theta, cudaStr
 // Q8_0 to f32, exactly: from split (qs, d) or from GGUF's 34-byte blocks
 void q8_to_f32_launch(const int8_t* qs, const __half* d, float* out, long long n, cudaStream_t st);
 void q8_raw_to_f32_launch(const uint8_t* raw, float* out, long long n, cudaStream_t st);
+// the epilogues of split-K GEMMs (PART [splits][n][N] fp32, summed in split order): q / k / v with
+// the per-head norms and RoPE on halves; x += the sum; h = silu(gate) * up (interleaved by 128)
+void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, const float* norm_q,
+                        const float* norm_k, const float2* rope, bf16* q, bf16* k, bf16* v, cudaStream_t st);
+void enc_resid_sum_launch(const float* part, int splits, int n, int w, float* x, cudaStream_t st);
+void enc_swiglu_sum_launch(const float* part, int splits, int n, int ffn, bf16* h, cudaStream_t st);
 
 // --- memory-bound kernels (elementwise.cu) ---
 // y[r] = LayerNorm(x[map(r)]) * (1 + scale[row kind]), bf16 out.  Row map as GemmEpi's.

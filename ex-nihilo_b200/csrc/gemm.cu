@@ -218,7 +218,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int num_m = (M + 255) / 256, num_n = N / C::BN;
-  const int num_tiles = num_m * num_n;
+  // split-K (EPI_F32 only): tile t + s * num_mn sums k-blocks [s * num_kb / splits, (s + 1) *
+  // num_kb / splits) of output tile t into rows s * M .. of the output (fp32 partials)
+  const int splits = ep.splits > 1 ? ep.splits : 1;
+  const int num_mn = num_m * num_n;
+  const int num_tiles = num_mn * splits;
   const int num_kb = K / KB;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
@@ -262,8 +266,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, group_m, mb, nb);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int sp = tile / num_mn;
+        tile_coords(tile - sp * num_mn, num_m, num_n, group_m, mb, nb);
+        const int kb1 = (sp + 1) * num_kb / splits;
+        for (int kb = sp * num_kb / splits; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
             ok = false;
             break;
@@ -306,7 +312,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int sp = tile / num_mn;
+        const int kbn = (sp + 1) * num_kb / splits - sp * num_kb / splits;  // k-blocks of this tile
+        for (int kb = 0; kb < kbn; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) {
             ok = false;
             break;
@@ -343,14 +351,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     int it = 0;
     for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
       int mb, nb;
-      tile_coords(tile, num_m, num_n, group_m, mb, nb);
+      const int sp = tile / num_mn;
+      tile_coords(tile - sp * num_mn, num_m, num_n, group_m, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, status, STATUS_TIMEOUT_GEMM)) break;
       tc_fence_after();
       const int row = mb * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::BN;
-      epilogue<256, EPI>(taddr, row, row < M, nb * C::BN, ep);
+      epilogue<256, EPI>(taddr, row + sp * M, row < M, nb * C::BN, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
@@ -444,7 +453,7 @@ static int launch_pair(const GemmArgs& g, int* d_status, int num_sms, cudaStream
   const uint32_t bb[2] = {BK, 128};
   if (make_tmap_bf16(&ta, g.a, 2, da, sa, ba) || make_tmap_bf16(&tb, g.b, 2, db, sb, bb)) return -4;
   const int num_m = (g.M + 255) / 256;
-  const int tiles = num_m * (g.N / C::BN);
+  const int tiles = num_m * (g.N / C::BN) * (g.ep.splits > 1 ? g.ep.splits : 1);
   int clusters = num_sms / 2;
   clusters = tiles < clusters ? tiles : clusters;
   int group_m = static_cast<int>((48ll << 20) / (256ll * g.K * 2));
@@ -509,12 +518,16 @@ int gemm_i8_launch(const GemmArgs& g, const int8_t* a, const int8_t* b, int* d_s
 
 int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.K % BK) return -1;
+  if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b)) & 15) return -1;
+  if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return -1;
+  if (g.ep.splits > 1) {  // split-K: fp32 partials from the pair kernel only
+    if (g.epi != EPI_F32 || !g.pairs || g.N % 256 || num_sms < 2 || g.ep.splits > g.K / BK) return -1;
+    return launch_pair<EPI_F32>(g, d_status, num_sms, st);
+  }
   if (g.epi == EPI_QKV) {  // whole heads a tile: q, k and v widths multiples of 256, N their sum
     const int kvw = g.ep.kv_width > 0 ? g.ep.kv_width : g.ep.width;
     if (g.ep.width <= 0 || g.ep.width % 256 || kvw % 256 || g.N != g.ep.width + 2 * kvw) return -1;
   }
-  if ((reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b)) & 15) return -1;
-  if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return -1;
   if (g.pairs && g.N % 256 == 0 && num_sms >= 2) {
     switch (g.epi) {
       case EPI_QKV:

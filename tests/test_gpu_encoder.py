@@ -43,10 +43,11 @@ def test_encoder_matches_transformers_golden(small, golden_dir, case):
     assert err < TOL
 
 
-@pytest.mark.parametrize("n", [1, 127, 300])
+@pytest.mark.parametrize("n", [1, 127, 300, 600])
 def test_encoder_matches_oracle(small, small_wt, n):
     """Lengths around the attention's 128-row tiles and 64-key units (one token; one tile short of
-    a row; three tiles, the last ragged), text positions."""
+    a row; three tiles, the last ragged), text positions; up to 512 tokens the GEMMs run split
+    along K with the epilogues after the sum, 600 tokens take the fused epilogues."""
     ids = EO.synth_ids(EO.SMALL, n, seed=n)
     got = small.states(ids)
     want = EO.states(small_wt, EO.SMALL, ids)
