@@ -67,6 +67,17 @@ __device__ __forceinline__ void conv_epilogue(uint32_t taddr, int row, bool vali
           v[4 * i + 3] += x.w;
         }
       }
+      if (e.dup) {  // DupUp3D (ref_vae.py:77-83): output channel o of sub-pixel (sy, sx) repeats
+                    // input channel f / rep, f = ((o ft + ft - 1) 2 + sy) 2 + sx, rep = 4 cout ft / ci
+        const int y = row / e.out_w, x = row - y * e.out_w, sy = y & 1, sx = x & 1;
+        const int rep = 4 * e.cout * e.dup_ft / e.dup_ci;
+        const float* src = e.dup + (static_cast<long long>(y >> 1) * (e.out_w >> 1) + (x >> 1)) * e.dup_ci;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int f = (((col + i) * e.dup_ft + e.dup_ft - 1) * 2 + sy) * 2 + sx;
+          v[i] += __ldg(src + f / rep);
+        }
+      }
       float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + static_cast<long long>(row) * e.ld_out + col);
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -298,6 +309,9 @@ int conv_launch(const ConvArgs& a, int* d_status, int num_sms, cudaStream_t st) 
   if (a.h <= 0 || a.w <= 0 || a.cp <= 0 || a.cp % BK || a.cout <= 0) return -1;
   if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.wt)) & 15) return -1;
   const int epi = a.ep.kind;
+  if (a.ep.dup && (epi != CONV_F32 || a.ep.out_w != a.w || (a.w | a.h) & 1 || a.ep.dup_ci <= 0 || a.ep.dup_ft < 1 ||
+                   (4 * a.cout * a.ep.dup_ft) % a.ep.dup_ci))
+    return -1;
   if (epi == CONV_RGBA) {
     if (a.taps != 9 || a.cout > 16) return -1;
     return conv_run<16, CONV_RGBA, 9>(a, d_status, num_sms, st);

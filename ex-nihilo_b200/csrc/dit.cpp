@@ -150,7 +150,6 @@ NcclApi& nccl() {
 struct SpBufs {
   void* mem = nullptr;       // one allocation, the same layout on every rank (peers address it by offset)
   int cap_nloc = 0, cap_ntot = 0, cap_p = 0, cap_n = 0, cap_wg = 0;
-  float* xp = nullptr;       // every prefix row's x on step 1 [P][W]
   bf16* qf = nullptr;        // this rank's heads, every row of the pass [n_tot][Wg]: every rank's QKV stores here
   bf16* att_in = nullptr;    // attention out of this rank's rows, all heads [n_loc][W]: every rank's attention
                              // stores its heads' columns here
@@ -893,7 +892,7 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
       off += al(bytes);
       return o;
     };
-    const size_t oxp = take(size_t(std::max(PP, 1)) * W * 4), oqf = take(size_t(NT) * Wg * 2),
+    const size_t oqf = take(size_t(NT) * Wg * 2),
                  oat = take(size_t(NL) * W * 2), orp = take(size_t(NL) * 64 * 8),
                  ozs = take(size_t(64) * (NN / G) * 4), oza = take(size_t(64) * NN * 4), obar = take(sizeof(int)),
                  oflg = take(kMaxSp * sizeof(int));
@@ -901,7 +900,6 @@ int ensure_sp(exn_handle* h, int n_loc, int n_tot, int P, int N, int L) {
     b.mem = nullptr;
     CK(cudaMalloc(&b.mem, off));
     char* m = static_cast<char*>(b.mem);
-    b.xp = reinterpret_cast<float*>(m + oxp);
     b.qf = reinterpret_cast<bf16*>(m + oqf);
     b.att_in = reinterpret_cast<bf16*>(m + oat);
     b.rope = reinterpret_cast<float2*>(m + orp);
@@ -976,31 +974,36 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
 
   // timestep
   if ((rc = timestep_chain(h, in.sigma))) return rc;
-  // first pass: every prefix row through txt_in (and an edit's picture through img_in), this rank's slice kept
+  // first pass: this rank's prefix rows [lo, hi) through txt_in (the text rows among them) and
+  // img_in (an edit picture's rows among them), straight into its x.  Prefix row of text row t: t
+  // before the picture's A rows, t + nref after them; the picture holds prefix rows [a, a + nref).
   if (!in.cached) {
-    if (in.ptext > 0) {
-      rms_launch(in.ctx, h->txt_norm, h->ctxn, in.ptext, c.context, h->st);
+    const int lo = r * pl, hi = lo + pl, a = in.nref ? in.a : in.ptext, nref = in.nref;
+    const int t0 = lo <= a ? lo : std::max(lo - nref, a), t1 = hi <= a ? hi : std::max(hi - nref, a);
+    if (t1 > t0) {
+      rms_launch(in.ctx + size_t(t0) * c.context, h->txt_norm, h->ctxn, t1 - t0, c.context, h->st);
       GemmEpi e1;
       e1.out = h->tin;
       e1.ld_out = W;
-      if ((rc = gemm(h, h->ctxn, c.context, h->w_txt_in, c.context, in.ptext, W, c.context, EPI_GELU_BF16, e1)))
+      if ((rc = gemm(h, h->ctxn, c.context, h->w_txt_in, c.context, t1 - t0, W, c.context, EPI_GELU_BF16, e1)))
         return rc;
       GemmEpi e2;
-      e2.out = b.xp;
+      e2.out = h->x;
       e2.ld_out = W;
-      e2.split_at = in.nref ? in.a : (1 << 30);
-      e2.split_gap = in.nref;
-      if ((rc = gemm(h, h->tin, W, h->w_txt_out, W, in.ptext, W, W, EPI_F32, e2))) return rc;
+      e2.off = (t0 < a ? t0 : t0 + nref) - lo;
+      e2.split_at = t0 < a ? a - t0 : (1 << 30);
+      e2.split_gap = nref;
+      if ((rc = gemm(h, h->tin, W, h->w_txt_out, W, t1 - t0, W, W, EPI_F32, e2))) return rc;
     }
-    if (in.nref) {
-      latent_rows_launch(in.ref, h->ref_rows, 1, c.latent, in.nref, h->st);
+    const int r0 = std::max(lo, a), r1 = std::min(hi, a + nref);
+    if (nref && r1 > r0) {
+      latent_rows_launch(in.ref, h->ref_rows, 1, c.latent, r1 - r0, h->st, nref, r0 - a);
       GemmEpi er;
-      er.out = b.xp;
+      er.out = h->x;
       er.ld_out = W;
-      er.off = in.a;
-      if ((rc = gemm(h, h->ref_rows, c.latent, h->w_img_in, c.latent, in.nref, W, c.latent, EPI_F32, er))) return rc;
+      er.off = r0 - lo;
+      if ((rc = gemm(h, h->ref_rows, c.latent, h->w_img_in, c.latent, r1 - r0, W, c.latent, EPI_F32, er))) return rc;
     }
-    CK(cudaMemcpyAsync(h->x, b.xp + size_t(r) * pl * W, size_t(pl) * W * 4, cudaMemcpyDeviceToDevice, h->st));
   }
   // this rank's image rows: latent columns [r N/G, (r+1) N/G)
   latent_rows_launch(in.lat, h->lat_rows, 1, c.latent, Nl, h->st, N, r * Nl);

@@ -171,6 +171,11 @@ struct ConvEpi {
   const float* bias = nullptr;  // [cout rounded up to 16]
   const float* res = nullptr;
   long long ld_res = 0;
+  // CONV_F32 of an upsampling convolution: + Wan's DupUp3D of the stage's input DUP f32
+  // [h/2][w/2][dup_ci] (the channel repeat and 2 x 2 pixel shuffle of the last of dup_ft frames),
+  // pixel (y, x) of the w-wide output reading input pixel (y/2, x/2)
+  const float* dup = nullptr;
+  int dup_ci = 0, dup_ft = 1, out_w = 0;
   int cout = 0;                 // set by conv_launch
 };
 struct ConvArgs {
@@ -193,8 +198,6 @@ void round_bf16_launch(float* v, long long n, cudaStream_t st);
 void vae_to_bf16_launch(const float* x, bf16* y, long long n, int c, int cp, cudaStream_t st);
 // u bf16 [2h][2w][cp]: x f32 [h][w][c] repeated 2 x 2 (nearest), channels c.. cp-1 zero
 void vae_up2_launch(const float* x, bf16* u, int h, int w, int c, int cp, cudaStream_t st);
-// y f32 [2h][2w][co] += DupUp3D(keep f32 [h][w][ci]) of the last of FT frames
-void vae_dupup_add_launch(const float* keep, float* y, int h, int w, int ci, int co, int ft, cudaStream_t st);
 // p bf16 [n][n] = softmax(s * scale) by rows of s f32 [n][n]
 void vae_softmax_launch(const float* s, bf16* p, int n, float scale, cudaStream_t st);
 // out bf16 [c][n] = in bf16 [n][c] (row stride ld_in)

@@ -390,7 +390,7 @@ const ConvW* cw(exn_vae* v, const std::string& prefix) {
 
 // out f32 [h w][o] = conv(x bf16 [h w][cp]) + bias (+ res); or bf16 / RGBA by KIND
 int conv(exn_vae* v, const std::string& prefix, const bf16* x, int h, int w, void* out, int kind,
-         const float* res = nullptr) {
+         const float* res = nullptr, const float* dup = nullptr, int dup_ci = 0, int dup_ft = 1) {
   const ConvW* c = cw(v, prefix);
   if (!c || !c->w || !c->b) return vfail(v, EXN_ENOWEIGHTS, "VAE tensor %s not loaded", prefix.c_str());
   ConvArgs a;
@@ -407,6 +407,10 @@ int conv(exn_vae* v, const std::string& prefix, const bf16* x, int h, int w, voi
   a.ep.bias = c->b;
   a.ep.res = res;
   a.ep.ld_res = c->o;
+  a.ep.dup = dup;
+  a.ep.dup_ci = dup_ci;
+  a.ep.dup_ft = dup_ft;
+  a.ep.out_w = w;
   const int r = conv_launch(a, v->d_status, v->sms, v->st);
   if (r) return vfail(v, EXN_ECUDA, "convolution %s (%d x %d, %d -> %d) launch failed: %d", prefix.c_str(), h, w, c->i,
                       c->o, r);
@@ -500,8 +504,8 @@ int decode(exn_vae* v, const float* d_latent, int h, int w, Scratch& sc) {
     if (st.up) {
       vae_up2_launch(x, sc.a, hh, ww, st.out, pad64(st.out), v->st);
       const std::string p = "decoder.upsamples." + std::to_string(s) + ".upsamples.3.resample.1";
-      if ((rc = conv(v, p, sc.a, 2 * hh, 2 * ww, y, CONV_F32))) return rc;
-      vae_dupup_add_launch(sc.keep, y, hh, ww, st.in, st.out, st.tup ? 2 : 1, v->st);
+      // the DupUp3D shortcut of the stage's input added in the convolution's epilogue
+      if ((rc = conv(v, p, sc.a, 2 * hh, 2 * ww, y, CONV_F32, nullptr, sc.keep, st.in, st.tup ? 2 : 1))) return rc;
       std::swap(x, y);
       hh *= 2;
       ww *= 2;

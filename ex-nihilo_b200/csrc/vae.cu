@@ -1,10 +1,11 @@
 // vae.cu -- the VAE decoder's memory-bound kernels, channels last: the
 // RMS norm (with SiLU) that feeds each convolution, the nearest 2x upsample,
-// Wan's DupUp3D shortcut of an upsampling stage, the attention's row softmax
-// and transpose, and the weights' reorder at load.  They replace the
-// reference's v_rms + x_silu, x_up2, x_dupup_add, x_softmax_rows,
+// the attention's row softmax and transpose, and the weights' reorder at
+// load.  They replace the reference's v_rms + x_silu, x_up2, x_softmax_rows,
 // x_transpose (src/cuda/vae.cu:143-214, illatio's v_rms; called from
 // src/cuda-vae.lisp:37-136) with the shapes of inspect/ref_vae.py:42-88.
+// Wan's DupUp3D shortcut (x_dupup_add) is added in the upsampling
+// convolution's epilogue (conv.cu).
 #include <math.h>
 
 #include "exn_device.cuh"
@@ -76,23 +77,6 @@ __global__ void k_vae_up2(const float* __restrict__ x, bf16* __restrict__ u, int
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
   if (ch < c) v = __ldg(reinterpret_cast<const float4*>(x + (static_cast<long long>(oy >> 1) * w + (ox >> 1)) * c + ch));
   reinterpret_cast<uint2*>(u)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-}
-
-// y [2h][2w][co] += DupUp3D(keep [h][w][ci]): ref_vae.py:77-83 for the last of FT frames: output
-// channel o at sub-pixel (sy, sx) is the flattened (o, frame ft - 1, sy, sx) index f of the channels
-// each repeated rep = co ft 4 / ci times, i.e. input channel f / rep
-__global__ void k_vae_dupup_add(const float* __restrict__ keep, float* __restrict__ y, int h, int w, int ci, int co,
-                                int ft) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = 4LL * h * w * co;
-  if (i >= total) return;
-  const int o = static_cast<int>(i % co);
-  const long long op = i / co;
-  const int ox = static_cast<int>(op % (2 * w)), oy = static_cast<int>(op / (2 * w));
-  const int sy = oy & 1, sx = ox & 1;
-  const int rep = co * ft * 4 / ci;
-  const int f = ((o * ft + (ft - 1)) * 2 + sy) * 2 + sx;
-  y[i] += __ldg(keep + (static_cast<long long>(oy >> 1) * w + (ox >> 1)) * ci + f / rep);
 }
 
 // one block of 256 threads per row: p = softmax(s * scale) (ref_vae.py:70-71), bf16 out
@@ -178,11 +162,6 @@ void vae_to_bf16_launch(const float* x, bf16* y, long long n, int c, int cp, cud
 void vae_up2_launch(const float* x, bf16* u, int h, int w, int c, int cp, cudaStream_t st) {
   const long long total = 4LL * h * w * (cp / 4);
   k_vae_up2<<<nblocks(total, 256), 256, 0, st>>>(x, u, h, w, c, cp);
-}
-
-void vae_dupup_add_launch(const float* keep, float* y, int h, int w, int ci, int co, int ft, cudaStream_t st) {
-  const long long total = 4LL * h * w * co;
-  k_vae_dupup_add<<<nblocks(total, 256), 256, 0, st>>>(keep, y, h, w, ci, co, ft);
 }
 
 void vae_softmax_launch(const float* s, bf16* p, int n, float scale, cudaStream_t st) {
