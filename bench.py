@@ -72,6 +72,16 @@ def picture_flops(batch=1, layers=LAYERS):
     return batch * g, batch * a
 
 
+def cfg3_flops(layers=LAYERS, p=256, h=64, w=96):
+    """Algorithmic FLOPs of one 8-step BASELINE config 3 picture (1536 x 1024: a 64 x 96 latent,
+    256 text rows)."""
+    n = h * w
+    g = gemm_flops_step(p + n, True, p=p, nimg=n, layers=layers) + 7 * gemm_flops_step(n, False, p=p, nimg=n,
+                                                                                        layers=layers)
+    a = attn_flops_step(True, p=p, nimg=n, layers=layers) + 7 * attn_flops_step(False, p=p, nimg=n, layers=layers)
+    return g, a
+
+
 def edit_flops(layers=LAYERS, p_text=512, a=8, rh=64, rw=64, h=H, w=WW):
     """Algorithmic FLOPs of one 8-step edit picture: the prefix is the text's
     p_text rows with the reference picture's rh*rw rows after its first A (src/host.lisp:37-50),
@@ -454,6 +464,39 @@ def run_exn(args):
         out["config"]["global_batch"] = args.pictures
     if args.layers != LAYERS:
         out["config"]["workload"] += " -- PROFILING CASE with %d of 32 blocks, not a bench number" % args.layers
+    # BASELINE config 3 on the same handle: one 1536 x 1024 picture (64 x 96 latent, 256 text rows)
+    if world == 1 and args.workload == "cfg2" and args.layers == LAYERS and not args.no_cfg3:
+        p3, h3, w3 = 256, 64, 96
+        c3, l3 = O.synth_inputs(O.Shape(), p3, h3, w3, seed=300)
+        c3_d = torch.from_numpy(np.ascontiguousarray(c3)).cuda()
+        z3_0 = torch.from_numpy(np.ascontiguousarray(l3)).cuda()
+        z3_d = torch.empty_like(z3_0)
+
+        def one3():
+            with torch.cuda.stream(stream):
+                z3_d.copy_(z3_0)
+            d.generate_device(1, c3_d.data_ptr(), p3, z3_d.data_ptr(), h3, w3, SIGMAS, stream=stream.cuda_stream)
+
+        for _ in range(2):
+            one3()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(3):
+            one3()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        d.sync()
+        ms3 = f0.elapsed_time(f1) / 3
+        g3, a3 = cfg3_flops()
+        out["cfg3_picture"] = {"workload": "BASELINE config 3: 1536 x 1024 picture (64 x 96 latent) + 256 text rows, "
+                                           "8 Euler steps",
+                               "ms_per_picture": round(ms3, 2), "images_per_s": round(1e3 / ms3, 4),
+                               "algorithmic_tflop": round((g3 + a3) / 1e12, 1),
+                               "tc_peak_frac": round((g3 + a3) / (ms3 * 1e-3) / 1e12 / bt, 4),
+                               "finite": bool(torch.isfinite(z3_d).all().item()),
+                               "timing": "CUDA events on the library's stream, inputs in HBM, 3 pictures after 2 "
+                                         "warm-up pictures"}
     # the step after the DiT: the VAE decoder on one picture's latent (rank 0, 1 GPU lines only)
     if world == 1 and not args.no_vae:
         v = E.Vae(device=local)
@@ -640,6 +683,7 @@ def main():
                     help="cfg2: one picture per GPU per step (default); cfg4: one 8704-row edit over all GPUs; "
                          "cfg5: 64 pictures split over the GPUs")
     ap.add_argument("--pictures", type=int, default=64, help="cfg5: pictures in the job")
+    ap.add_argument("--no-cfg3", action="store_true", help="skip the config 3 picture timing (1 GPU lines)")
     ap.add_argument("--no-vae", action="store_true",
                     help="skip the VAE decoder and prompt encoder timings (1 GPU lines)")
     ap.add_argument("--no-sp-edit", action="store_true",
