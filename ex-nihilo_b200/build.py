@@ -22,7 +22,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libexn_b200.so")
-SOURCES = ["gemm.cu", "gemm_q8.cu", "conv.cu", "attention.cu", "elementwise.cu", "vae.cu", "encoder.cu", "noalloc.cu",
+SOURCES = ["gemm.cu", "gemm_q8.cu", "gemm_thin.cu", "conv.cu", "attention.cu", "elementwise.cu", "vae.cu", "encoder.cu", "noalloc.cu",
            "dit.cpp", "vae.cpp", "encoder.cpp", "gguf.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

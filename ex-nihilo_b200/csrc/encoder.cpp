@@ -302,9 +302,16 @@ int splits(const exn_enc* e, int n, int N, int K) {
   return split_for(((n + 255) / 256) * (N / 256), K / 64, e->sms / 2);
 }
 
-// a split-K GEMM of A [n][K] and B [N][K] into the partials of S
+// a split-K GEMM of A [n][K] and B [N][K] into the partials of S: up to 256 tokens with the weights
+// as the 256-row MMA operand (gemm_thin.cu), longer prompts on the pair GEMM
 int gemm_split(exn_enc* e, const bf16* a, const bf16* b, int n, int N, int K, int parts, const Scratch& s,
                const char* what, int layer) {
+  if (n <= 256) {
+    const int r = gemm_thin_launch(a, n, b, N, K, parts, s.part, e->d_status, e->sms, e->st);
+    if (r) return efail(e, EXN_ECUDA, "encoder block %d: %s GEMM (%d x %d x %d, thin) launch failed: %d", layer, what,
+                        n, N, K, r);
+    return EXN_OK;
+  }
   GemmArgs g;
   g.a = a;
   g.lda = K;
@@ -480,6 +487,7 @@ int exn_enc_open(const exn_enc_config* cfg, exn_enc** out) {
     ECK(cudaMemset(e->d_status, 0, sizeof(int)));
     ECK(static_cast<cudaError_t>(gemm_prepare()));
     ECK(static_cast<cudaError_t>(attention_prepare()));
+    ECK(static_cast<cudaError_t>(gemm_thin_prepare()));
     ECK(cudaEventCreate(&e->ev[0]));
     ECK(cudaEventCreate(&e->ev[1]));
     // weights: one bf16 slab for every block's matrices, one fp32 array for the vectors

@@ -142,6 +142,13 @@ int gemm_q8_launch(const GemmArgs& g, const int8_t* qs, const __half* dk, int* d
                    cudaStream_t st);
 int q8_scales_by_kblock_launch(const __half* d, __half* out, int n, int k, cudaStream_t st);
 
+// Thin activations (gemm_thin.cu): part [s][n][N] fp32 = X [n][K] W^T over part s of the k-blocks
+// (SPLITS parts), with the weights W [N][K] as the 256-row MMA operand; n <= 256, N a multiple of
+// 256.  0, -1 (bad shape), -4 (tensor map) or a cudaError_t.
+int gemm_thin_launch(const bf16* x, int n, const bf16* w, int N, int K, int splits, float* part, int* d_status,
+                     int num_sms, cudaStream_t st);
+int gemm_thin_prepare();
+
 // Scratch that needs no allocation (noalloc.cu): a RoPE table of at most kNoAllocMaxRows sequence
 // rows in a fixed device array.  Its address on DEVICE, which must be the current device: looked up
 // on the first call for that device, then cached.  0, -1 (bad argument) or a cudaError_t.
