@@ -329,13 +329,18 @@ int gemm_split(exn_enc* e, const bf16* a, const bf16* b, int n, int N, int K, in
 
 // one block of the text model over the N rows of S (x updated in place).  A thin prompt's GEMMs
 // run split along K into fp32 partials, summed (in split order) by the kernel that applies the
-// epilogue; a longer prompt's have the epilogue fused.
-int block(exn_enc* e, int li, int n, const Scratch& s) {
+// epilogue; a longer prompt's have the epilogue fused.  After a split residual GEMM the summing
+// kernel also writes the next RMS norm's output.  *NORMED: on entry, whether s.xn already holds
+// this block's attn_norm output; on return, whether it holds the next block's.
+int block(exn_enc* e, int li, int n, const Scratch& s, bool* normed) {
   const exn_enc_config& c = e->cfg;
   const EncLayer& L = e->layers[li];
+  const float* next_norm = li + 1 < c.layers ? e->layers[li + 1].attn_norm : nullptr;
   const int q = q_width(c), kv = kv_width(c);
   int rc, sp;
-  rms_launch(s.x, L.attn_norm, s.xn, n, c.width, e->st);
+  if (!*normed) rms_launch(s.x, L.attn_norm, s.xn, n, c.width, e->st);
+  *normed = false;
+  bool ffn_normed = false;
   if ((sp = splits(e, n, q + 2 * kv, c.width)) > 1) {
     if ((rc = gemm_split(e, s.xn, L.qkv, n, q + 2 * kv, c.width, sp, s, "q/k/v", li))) return rc;
     enc_qkv_sum_launch(s.part, sp, n, q, kv, L.q_norm, L.k_norm, s.rope, s.q, s.k, s.v, e->st);
@@ -382,7 +387,8 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
   }
   if ((sp = splits(e, n, c.width, q)) > 1) {
     if ((rc = gemm_split(e, s.xn, L.o, n, c.width, q, sp, s, "attn_output", li))) return rc;
-    enc_resid_sum_launch(s.part, sp, n, c.width, s.x, e->st);
+    enc_resid_rms_launch(s.part, sp, n, c.width, s.x, L.ffn_norm, s.xn, e->st);
+    ffn_normed = true;
   } else {  // x += attn Wo^T
     GemmArgs g;
     g.a = s.xn;
@@ -398,7 +404,7 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
     g.ep.mod = e->ones;
     if ((rc = gemm(e, g, "attn_output", li))) return rc;
   }
-  rms_launch(s.x, L.ffn_norm, s.xn, n, c.width, e->st);
+  if (!ffn_normed) rms_launch(s.x, L.ffn_norm, s.xn, n, c.width, e->st);
   if ((sp = splits(e, n, 2 * c.ffn, c.width)) > 1) {
     if ((rc = gemm_split(e, s.xn, L.gu, n, 2 * c.ffn, c.width, sp, s, "ffn_gate/up", li))) return rc;
     enc_swiglu_sum_launch(s.part, sp, n, c.ffn, s.h, e->st);
@@ -418,7 +424,8 @@ int block(exn_enc* e, int li, int n, const Scratch& s) {
   }
   if ((sp = splits(e, n, c.width, c.ffn)) > 1) {
     if ((rc = gemm_split(e, s.h, L.down, n, c.width, c.ffn, sp, s, "ffn_down", li))) return rc;
-    enc_resid_sum_launch(s.part, sp, n, c.width, s.x, e->st);
+    enc_resid_rms_launch(s.part, sp, n, c.width, s.x, next_norm, s.xn, e->st);
+    *normed = next_norm != nullptr;
   } else {  // x += h Wd^T
     GemmArgs g;
     g.a = s.h;
@@ -677,8 +684,9 @@ int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positio
   enc_embed_launch(e->embed, s.ids, s.x, n, e->cfg.width, e->st);
   enc_rope_launch(s.pos, s.rope, n, e->cfg.theta, e->st);
   ECK(cudaGetLastError());
+  bool normed = false;
   for (int li = 0; li < e->cfg.layers; ++li)
-    if ((rc = block(e, li, n, s))) return rc;
+    if ((rc = block(e, li, n, s, &normed))) return rc;
   ECK(cudaMemcpyAsync(states, s.x, static_cast<size_t>(n) * e->cfg.width * 4, cudaMemcpyDeviceToHost, e->st));
   ECK(cudaEventRecord(e->ev[1], e->st));
   if ((rc = enc_status(e))) return rc;

@@ -97,26 +97,61 @@ __global__ void k_enc_qkv_sum(const float* __restrict__ part, int splits, int n,
   for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
 }
 
-// x [n][w] += the sum of the partials
-__global__ void k_enc_resid_sum(const float* __restrict__ part, int splits, long long count, float* __restrict__ x) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= count / 4) return;
-  const float4* p = reinterpret_cast<const float4*>(part);
-  float4 a = p[i];
-  for (int sp = 1; sp < splits; ++sp) {
-    const float4 b = p[sp * (count / 4) + i];
-    a.x += b.x;
-    a.y += b.y;
-    a.z += b.z;
-    a.w += b.w;
+// one block of 256 threads a row: x [n][w] += the sum of the partials, then (NORM given) xn bf16 =
+// x / sqrt(mean(x^2) + 1e-6) * norm, the next GEMM's operand; w <= 4096, a multiple of 4
+__global__ void __launch_bounds__(256) k_enc_resid_rms(const float* __restrict__ part, int splits, int n, int w,
+                                                       float* __restrict__ x, const float* __restrict__ norm,
+                                                       bf16* __restrict__ xn) {
+  __shared__ float red[8];
+  const int r = blockIdx.x;
+  const int w4 = w / 4;
+  const long long stride4 = static_cast<long long>(n) * w4;
+  const float4* p = reinterpret_cast<const float4*>(part) + static_cast<long long>(r) * w4;
+  float4* xr = reinterpret_cast<float4*>(x) + static_cast<long long>(r) * w4;
+  float4 v[4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = threadIdx.x + 256 * i;
+    if (c < w4) {
+      float4 a = p[c];
+      for (int sp = 1; sp < splits; ++sp) {
+        const float4 b = p[sp * stride4 + c];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+      }
+      float4 o = xr[c];
+      o.x += a.x;
+      o.y += a.y;
+      o.z += a.z;
+      o.w += a.w;
+      xr[c] = o;
+      v[i] = o;
+      ss += (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w);
+    }
   }
-  float4* xp = reinterpret_cast<float4*>(x) + i;
-  float4 o = *xp;
-  o.x += a.x;
-  o.y += a.y;
-  o.z += a.z;
-  o.w += a.w;
-  *xp = o;
+  if (norm == nullptr) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  const float inv = rsqrtf(t / static_cast<float>(w) + 1e-6f);
+  uint2* y = reinterpret_cast<uint2*>(xn + static_cast<long long>(r) * w);
+  const float4* nw = reinterpret_cast<const float4*>(norm);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = threadIdx.x + 256 * i;
+    if (c < w4) {
+      const float4 m = __ldg(nw + c);
+      y[c] = make_uint2(pack_bf16x2(v[i].x * inv * m.x, v[i].y * inv * m.y),
+                        pack_bf16x2(v[i].z * inv * m.z, v[i].w * inv * m.w));
+    }
+  }
 }
 
 // h [n][ffn] bf16 = silu(gate) * up, the partials' columns gate and up interleaved by 128
@@ -160,9 +195,9 @@ void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, c
   k_enc_qkv_sum<<<blocks(warps * 32, 256), 256, 0, st>>>(part, splits, n, qw, kvw, norm_q, norm_k, rope, q, k, v);
 }
 
-void enc_resid_sum_launch(const float* part, int splits, int n, int w, float* x, cudaStream_t st) {
-  const long long count = static_cast<long long>(n) * w;
-  k_enc_resid_sum<<<blocks(count / 4, 256), 256, 0, st>>>(part, splits, count, x);
+void enc_resid_rms_launch(const float* part, int splits, int n, int w, float* x, const float* norm, bf16* xn,
+                          cudaStream_t st) {
+  k_enc_resid_rms<<<n, 256, 0, st>>>(part, splits, n, w, x, norm, xn);
 }
 
 void enc_swiglu_sum_launch(const float* part, int splits, int n, int ffn, bf16* h, cudaStream_t st) {

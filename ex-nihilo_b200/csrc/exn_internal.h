@@ -221,10 +221,12 @@ void enc_rope_launch(const int* pos, float2* table, int n, double theta, cudaStr
 void q8_to_f32_launch(const int8_t* qs, const __half* d, float* out, long long n, cudaStream_t st);
 void q8_raw_to_f32_launch(const uint8_t* raw, float* out, long long n, cudaStream_t st);
 // the epilogues of split-K GEMMs (PART [splits][n][N] fp32, summed in split order): q / k / v with
-// the per-head norms and RoPE on halves; x += the sum; h = silu(gate) * up (interleaved by 128)
+// the per-head norms and RoPE on halves; h = silu(gate) * up (interleaved by 128)
 void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, const float* norm_q,
                         const float* norm_k, const float2* rope, bf16* q, bf16* k, bf16* v, cudaStream_t st);
-void enc_resid_sum_launch(const float* part, int splits, int n, int w, float* x, cudaStream_t st);
+// x += the sum, then (NORM not null) xn = RMSNorm(x) * NORM in bf16 (the next GEMM's operand); w <= 4096
+void enc_resid_rms_launch(const float* part, int splits, int n, int w, float* x, const float* norm, bf16* xn,
+                          cudaStream_t st);
 void enc_swiglu_sum_launch(const float* part, int splits, int n, int ffn, bf16* h, cudaStream_t st);
 
 // --- memory-bound kernels (elementwise.cu) ---
