@@ -664,8 +664,15 @@ int exn_enc_load_gguf(exn_enc* e, const char* path) {
   return rc;
 }
 
-int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, float* states) {
-  if (!e || !ids || !states) return efail(e, EXN_EINVAL, "exn_enc_states: null argument");
+}  // extern "C"
+
+namespace {
+
+// The pass of exn_enc_states: rows SKIP .. N-1 of the states into OUT, host memory or (DEVICE)
+// device memory of the encoder's device, the pass ordered after what USER's stream holds
+int run_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, int skip, float* out, bool device,
+               cudaStream_t user) {
+  if (!e || !ids || !out) return efail(e, EXN_EINVAL, "exn_enc_states: null argument");
   if (n < 1 || n > kMaxTokens) return efail(e, EXN_EINVAL, "exn_enc_states: %d tokens (1 .. %d)", n, kMaxTokens);
   if (!exn_enc_weights_ready(e)) return efail(e, EXN_ENOWEIGHTS, "exn_enc_states: the encoder's weights are not loaded");
   for (int i = 0; i < n; ++i)
@@ -675,9 +682,18 @@ int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positio
   for (int i = 0; i < n; ++i)
     for (int a = 0; a < 3; ++a) pos[3 * i + a] = positions ? positions[3 * i + a] : i;
   ECK(cudaSetDevice(e->cfg.device));
+  if (skip < 0 || skip >= n) return efail(e, EXN_EINVAL, "exn_enc_states: skip %d of %d tokens", skip, n);
   Scratch s;
   int rc;
   if ((rc = ensure_scratch(e, n, &s))) return rc;
+  if (device) {  // after the caller's queued work (NULL: CUDA's default stream)
+    cudaEvent_t ue;
+    ECK(cudaEventCreateWithFlags(&ue, cudaEventDisableTiming));
+    const cudaError_t r1 = cudaEventRecord(ue, user);
+    const cudaError_t r2 = r1 == cudaSuccess ? cudaStreamWaitEvent(e->st, ue, 0) : r1;
+    cudaEventDestroy(ue);
+    ECK(r2);
+  }
   ECK(cudaEventRecord(e->ev[0], e->st));
   ECK(cudaMemcpyAsync(s.ids, ids, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, e->st));
   ECK(cudaMemcpyAsync(s.pos, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, e->st));
@@ -687,13 +703,28 @@ int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positio
   bool normed = false;
   for (int li = 0; li < e->cfg.layers; ++li)
     if ((rc = block(e, li, n, s, &normed))) return rc;
-  ECK(cudaMemcpyAsync(states, s.x, static_cast<size_t>(n) * e->cfg.width * 4, cudaMemcpyDeviceToHost, e->st));
+  const size_t w = e->cfg.width;
+  ECK(cudaMemcpyAsync(out, s.x + static_cast<size_t>(skip) * w, static_cast<size_t>(n - skip) * w * 4,
+                      device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, e->st));
   ECK(cudaEventRecord(e->ev[1], e->st));
   if ((rc = enc_status(e))) return rc;
   float ms = 0;
   ECK(cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]));
   e->last_ms = ms;
   return EXN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, float* states) {
+  return run_states(e, ids, n, positions, 0, states, false, nullptr);
+}
+
+int exn_enc_states_device(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, int skip,
+                          float* d_states, void* stream) {
+  return run_states(e, ids, n, positions, skip, d_states, true, static_cast<cudaStream_t>(stream));
 }
 
 int exn_enc_release(exn_enc* e) {

@@ -112,6 +112,8 @@ def lib():
         "exn_enc_weights_ready": (ctypes.c_int, [H]),
         "exn_enc_states": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_int32), fp]),
+        "exn_enc_states_device": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
+                                                 ctypes.POINTER(ctypes.c_int32), ctypes.c_int, vp, vp]),
         "exn_enc_release": (ctypes.c_int, [H]),
         "exn_test_enc_last_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
         "exn_test_enc_weights_digest": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_uint64)]),
@@ -447,6 +449,21 @@ class Encoder:
         self._ck(lib().exn_enc_states(self.h, ids.ctypes.data_as(ip), n,
                                       pos.ctypes.data_as(ip) if pos is not None else None, _fp(out)))
         return out
+
+    def states_device(self, ids, d_states, positions=None, skip=0, stream=None):
+        """encode-prompt's states into device memory (a pointer, e.g. a torch tensor's data_ptr()):
+        rows SKIP.. of the states, ready for Dit.generate_device as its context."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        n = len(ids)
+        pos = None
+        if positions is not None:
+            pos = np.ascontiguousarray(positions, dtype=np.int32)
+            if pos.shape != (n, 3):
+                raise ExnError(1, "positions must be (n, 3), got %s" % (pos.shape,))
+        ip = ctypes.POINTER(ctypes.c_int32)
+        self._ck(lib().exn_enc_states_device(self.h, ids.ctypes.data_as(ip), n,
+                                             pos.ctypes.data_as(ip) if pos is not None else None, skip,
+                                             ctypes.c_void_p(d_states), ctypes.c_void_p(stream)))
 
     def release(self):
         self._ck(lib().exn_enc_release(self.h))

@@ -233,6 +233,14 @@ int exn_enc_weights_ready(const exn_enc* e);
  * floats, row-major. */
 int exn_enc_states(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, float* states);
 
+/* encode-prompt's states without the host (src/encoder.lisp:55-67, whose states cross the host on
+ * their way to the DiT): rows SKIP .. N-1 (the system turn's SKIP rows cut) into D_STATES, device
+ * memory of the encoder's device, (N - SKIP) x width floats -- the context exn_generate_device
+ * takes.  Ordered after what STREAM (a cudaStream_t, NULL = CUDA's default stream) holds; the
+ * states are in place when the call returns. */
+int exn_enc_states_device(exn_enc* e, const int32_t* ids, int n, const int32_t* positions, int skip,
+                          float* d_states, void* stream);
+
 /* The encoder's scratch freed (the weights stay). */
 int exn_enc_release(exn_enc* e);
 

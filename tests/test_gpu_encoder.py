@@ -149,3 +149,28 @@ def test_encoder_full_model_prompt():
             ms.append(e.last_ms())
     assert s.shape == (141, 4096) and np.isfinite(s).all()
     print("\nencoder, 36 blocks, 141 tokens: %.2f ms a prompt on the device (best of 3)" % min(ms))
+
+
+def test_encoder_states_device_feed_the_dit():
+    """encode-prompt to the DiT without the host: exn_enc_states_device writes the states after the
+    system turn's rows into device memory, exn_generate_device reads them as its context, and the
+    8-step latent is bit for bit the one the host path gives (states to host, then exn_generate)."""
+    import torch
+    enc_shape = dict(width=256, layers=2, heads=2, kv_heads=2, ffn=512, vocab=512)
+    n, skip, h, w = 20, 4, 4, 6
+    ids = EO.synth_ids(EO.EncShape(**enc_shape), n, seed=11)
+    with E.Encoder(**enc_shape) as enc, E.Dit(width=256, layers=2, ffn=768, context=256) as dit:
+        enc.load_synthetic(1)
+        dit.load_synthetic(1)
+        _, lat = O.synth_inputs(O.Shape(width=256, layers=2, ffn=768, context=256), n - skip, h, w, seed=3)
+        z_host = dit.generate(enc.states(ids)[skip:], n - skip, lat[0], h, w)
+        ctx_d = torch.full((n - skip, 256), float("nan"), dtype=torch.float32, device="cuda")
+        enc.states_device(ids, ctx_d.data_ptr(), skip=skip)
+        z_d = torch.from_numpy(np.ascontiguousarray(lat[0])).cuda()
+        dit.generate_device(1, ctx_d.data_ptr(), n - skip, z_d.data_ptr(), h, w)
+        torch.cuda.synchronize()
+        assert np.array_equal(ctx_d.cpu().numpy(), enc.states(ids)[skip:])
+        assert np.array_equal(z_d.cpu().numpy(), z_host)
+        with pytest.raises(E.ExnError):
+            enc.states_device(ids, ctx_d.data_ptr(), skip=n)
+
