@@ -174,6 +174,26 @@ def test_full_eight_steps_match_ref_dit(full, inputs):
     assert O.rel_l2(z, g["z"]) < 0.045
 
 
+def test_full_cfg3_eight_steps_match_ref_dit(full):
+    """BASELINE config 3 end to end: 1536 x 1024 (a 64 x 96 latent, whose RoPE centring differs per
+    axis) with 256 text rows, the 8 Euler steps against ref_dit.py's own trajectory
+    (tests/golden/cfg3_euler.npz, made from the same synthetic weights and inputs): cosine >= 0.999,
+    latent rel-L2 < 0.045 as for config 2."""
+    import hashlib
+    g = np.load(os.path.join(os.path.dirname(GOLDEN), "cfg3_euler.npz"))
+    p3, h3, w3 = 256, 64, 96
+    ctx, lat = O.synth_inputs(O.Shape(), p3, h3, w3, seed=0)
+    assert hashlib.sha256(np.ascontiguousarray(lat).tobytes()).hexdigest() == str(g["lat_sha256"])
+    v = full.velocity(ctx[0], p3, lat[0], h3, w3, float(O.TURBO_SIGMAS[0]))
+    z = full.generate(ctx[0], p3, lat[0], h3, w3, O.TURBO_SIGMAS, prefix_key="cfg3")
+    print("\nconfig 3: first velocity cosine %.6f rel-L2 %.4f; 8-step latent cosine %.6f rel-L2 %.4f"
+          % (O.cosine(v, g["v_first"]), O.rel_l2(v, g["v_first"]), O.cosine(z, g["z"]), O.rel_l2(z, g["z"])))
+    assert np.isfinite(z).all()
+    assert O.cosine(v, g["v_first"]) >= 0.999
+    assert O.cosine(z, g["z"]) >= 0.999
+    assert O.rel_l2(z, g["z"]) < 0.045
+
+
 def test_full_cached_prefix_equals_recomputed(full, inputs):
     ctx, lat = inputs
     full.velocity(ctx[1], P, lat[1], H, W, 1.0, prefix_key="p1")
