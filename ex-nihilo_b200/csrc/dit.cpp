@@ -176,7 +176,8 @@ struct exn_handle {
   // attention work split (AttnArgs::split_mode, EXN_ATT_SINGLE at open) and the SM count it plans
   // for (0: the device's); a testing entry point may change both
   int att_mode = 2, att_sms = 0;
-  // GEMM tiles: 1 256 x 256 on CTA pairs (EXN_GEMM_PAIRS=0 at open: 128-row tiles of one CTA)
+  // GEMM tiles (GemmArgs::pairs; EXN_GEMM_PAIRS at open): 1 256 x 256 on CTA pairs, narrower
+  // one-CTA tiles where pair tiles would not fill one round; 2 pairs only; 0 one-CTA tiles
   int gemm_pairs = 1;
   cudaStream_t st = nullptr;
   std::string err;
@@ -1266,7 +1267,7 @@ int exn_open(const exn_config* cfg, exn_handle** out) {
   for (size_t i = 0; i < h->spec.size(); ++i) h->index[h->spec[i].name] = static_cast<int>(i);
   h->loaded.assign(h->spec.size(), 0);
   h->prof.on = std::getenv("EXN_PROFILE") != nullptr;
-  if (const char* e = std::getenv("EXN_GEMM_PAIRS")) h->gemm_pairs = std::atoi(e) != 0;
+  if (const char* e = std::getenv("EXN_GEMM_PAIRS")) h->gemm_pairs = std::atoi(e);
   if (const char* e = std::getenv("EXN_ATT_SINGLE")) h->att_mode = std::atoi(e) == 1 ? 1 : (std::atoi(e) == 0 ? 0 : 2);
   *out = h;
   return EXN_OK;
@@ -1755,7 +1756,8 @@ int exn_test_comm_stats(exn_handle* h, long long* settles, long long* sleeps, do
 
 int exn_test_gemm_pairs(exn_handle* h, int pairs) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_gemm_pairs: null handle");
-  h->gemm_pairs = pairs != 0;
+  if (pairs < 0 || pairs > 2) return fail(h, EXN_EINVAL, "exn_test_gemm_pairs: mode %d", pairs);
+  h->gemm_pairs = pairs;
   return EXN_OK;
 }
 

@@ -99,7 +99,9 @@ struct GemmArgs {
   int M = 0, N = 0, K = 0;
   int epi = EPI_F32;
   GemmEpi ep;
-  // tile shape: 1 (default) 256 x 256 tiles on CTA pairs where N allows, 0 128-row tiles of one CTA
+  // tile shape: 1 (default) 256 x 256 tiles on CTA pairs where N allows, one-CTA tiles of fewer
+  // columns where pair tiles would not fill one round; 2 pairs where N allows; 0 128-row tiles of
+  // one CTA
   int pairs = 1;
 };
 

@@ -528,7 +528,12 @@ int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) 
     const int kvw = g.ep.kv_width > 0 ? g.ep.kv_width : g.ep.width;
     if (g.ep.width <= 0 || g.ep.width % 256 || kvw % 256 || g.N != g.ep.width + 2 * kvw) return -1;
   }
-  if (g.pairs && g.N % 256 == 0 && num_sms >= 2) {
+  // CTA pairs for 256 x 256 tiles where N allows -- unless (pairs 1) those tiles would not fill one
+  // round of the SM pairs and the epilogue has a narrower one-CTA tile that does: then 128-row tiles
+  // of 64 (F32, BF16) or 128 (GATE_RESID) columns (every tile shape gives the same bits)
+  const bool narrow = g.pairs == 1 && (g.epi == EPI_F32 || g.epi == EPI_BF16 || g.epi == EPI_GATE_RESID) &&
+                      ((g.M + 255) / 256) * (g.N / 256) < num_sms / 2;
+  if (g.pairs && !narrow && g.N % 256 == 0 && num_sms >= 2) {
     switch (g.epi) {
       case EPI_QKV:
         if (g.ep.width % 256) return -1;
@@ -552,15 +557,15 @@ int gemm_launch(const GemmArgs& g, int* d_status, int num_sms, cudaStream_t st) 
       if (g.N != 64) return -1;
       return launch_bn<64, EPI_PROJ>(g, d_status, num_sms, st);
     case EPI_GATE_RESID:
-      if (g.N % 256 == 0) return launch_bn<256, EPI_GATE_RESID>(g, d_status, num_sms, st);
+      if (g.N % 256 == 0 && !narrow) return launch_bn<256, EPI_GATE_RESID>(g, d_status, num_sms, st);
       if (g.N % 128 == 0) return launch_bn<128, EPI_GATE_RESID>(g, d_status, num_sms, st);
       return -1;
     case EPI_F32:
-      if (g.N % 256 == 0) return launch_bn<256, EPI_F32>(g, d_status, num_sms, st);
+      if (g.N % 256 == 0 && !narrow) return launch_bn<256, EPI_F32>(g, d_status, num_sms, st);
       if (g.N % 64 == 0) return launch_bn<64, EPI_F32>(g, d_status, num_sms, st);
       return -1;
     case EPI_BF16:
-      if (g.N % 256 == 0) return launch_bn<256, EPI_BF16>(g, d_status, num_sms, st);
+      if (g.N % 256 == 0 && !narrow) return launch_bn<256, EPI_BF16>(g, d_status, num_sms, st);
       if (g.N % 64 == 0) return launch_bn<64, EPI_BF16>(g, d_status, num_sms, st);
       return -1;
     case EPI_GELU_BF16:

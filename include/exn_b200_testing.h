@@ -48,7 +48,9 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
 int exn_test_comm_stats(exn_handle* h, long long* settles, long long* sleeps, double* seconds);
 
 /* The GEMM tiles of this handle's later calls: PAIRS 1 (the default) 256 x 256 tiles on CTA pairs
- * wherever N is a multiple of 256, 0 128-row tiles of one CTA everywhere. */
+ * wherever N is a multiple of 256, except where those would not fill one round of the SM pairs and
+ * a narrower one-CTA tile does (epilogues F32, BF16, gated residual); 2 pairs wherever N allows;
+ * 0 128-row tiles of one CTA everywhere. */
 int exn_test_gemm_pairs(exn_handle* h, int pairs);
 
 /* How the attention kernel splits its work, for this handle's later calls: MODE 2 (the default)

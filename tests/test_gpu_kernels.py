@@ -39,17 +39,20 @@ def test_gemm_matches_fp64(dit, m, n, k):
     assert err < 1e-5, err
 
 
-@pytest.mark.parametrize("epi_shape", [(300, 512, 4096), (1088, 4096, 4096), (513, 12288, 4096)])
+@pytest.mark.parametrize("epi_shape", [(300, 512, 4096), (1088, 4096, 4096), (513, 12288, 4096),
+                                       (576, 4096, 4096)])
 def test_gemm_tile_shapes_are_bit_identical(dit, epi_shape):
-    """256 x 256 tiles on CTA pairs and 128-row tiles of one CTA give every output element the same
-    bits (the same k-order of the same MMAs), so a rank may pick either without changing a row."""
+    """256 x 256 tiles on CTA pairs (mode 2), 128-row tiles of one CTA (mode 0) and the default
+    (mode 1: pairs, or 128 x 64 one-CTA tiles where pair tiles would not fill one round -- 300 and
+    576 rows here) give every output element the same bits (the same k-order of the same MMAs), so
+    a rank may pick any without changing a row."""
     m, n, k = epi_shape
     g = torch.Generator().manual_seed(m + n)
     a = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
     b = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16).cuda()
     outs = []
     try:
-        for pairs in (1, 0):
+        for pairs in (1, 2, 0):
             dit._ck(E.lib().exn_test_gemm_pairs(dit.h, pairs))
             c = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
             dit._ck(E.lib().exn_test_gemm(dit.h, a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k))
@@ -57,7 +60,7 @@ def test_gemm_tile_shapes_are_bit_identical(dit, epi_shape):
     finally:
         dit._ck(E.lib().exn_test_gemm_pairs(dit.h, 1))
     assert torch.isfinite(outs[0]).all()
-    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
 
 
 def q8_weights(n, k, seed):
