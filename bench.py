@@ -389,7 +389,8 @@ def run_exn(args):
               "ms_per_picture": round(sp_ms, 2), "images_per_s": round(1e3 / sp_ms, 4),
               "e2e_ms_per_picture": round(sp_e2e, 2), "steps": 3, "warmup": 3, "scaling": "strong",
               "timing": "CUDA events on the library's stream around each exn_generate's device part, max over ranks",
-              "rank0_host_waits": getattr(edit_pictures, "host_waits", None)}
+              "rank0_host_waits": getattr(edit_pictures, "host_waits", None),
+              "rank0_classes": getattr(edit_pictures, "classes", None)}
     if rank != 0:
         d.close()
         return None
@@ -585,6 +586,16 @@ def edit_pictures(d, rank, world, dist, steps, warmup):
                                 "wait_ms_per_picture": round((s1[2] - s0[2]) * 1e3 / steps, 3)}
     ms = max_over_ranks(dist, dev_ms / steps)
     e2e_ms = max_over_ranks(dist, dt * 1e3)
+    # the kernel classes of one more picture on this rank (every rank runs it: the same calls in order)
+    d.profile(True)
+    d.generate(ctx[0], p_text, lat[0], H, WW, SIGMAS, prefix_key=("prof", 0), ref=refarg)
+    prof = d.last_profile()
+    d.profile(False)
+    edit_pictures.classes = {"gemm_ms": round(prof["gemm_ms"], 2), "attention_ms": round(prof["attn_ms"], 2),
+                             "barrier_ms": round(prof["barrier_ms"], 2), "other_ms": round(prof["other_ms"], 2),
+                             "timing": "CUDA events on rank 0's library stream around each kernel class, one "
+                                       "more picture; barrier = from the end of the kernel before each pass "
+                                       "barrier to the start of the one after (the wait for the slowest rank)"}
     if world > 1:
         d.comm_destroy()
     barrier(dist)
@@ -631,6 +642,7 @@ def run_edit(args):
                 "h2d_bytes_per_step": (p_text * CTX + 2 * LAT * H * WW) * 4, "d2h_bytes_per_step": LAT * H * WW * 4},
         "clocks": clk.summary(),
         "gpu_launches": launches,
+        "rank0_classes": getattr(edit_pictures, "classes", None),
     }
 
 

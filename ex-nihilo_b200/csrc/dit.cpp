@@ -219,7 +219,8 @@ struct exn_handle {
   float* trace_host = nullptr;
   size_t trace_floats = 0;
   Profile prof;
-  double last_ms[4] = {0, 0, 0, 0};  // GEMM (other than gate_up), attention, other, gate_up GEMM
+  // GEMM (other than gate_up), attention, other, gate_up GEMM, sequence-parallel barriers
+  double last_ms[5] = {0, 0, 0, 0, 0};
   // device time of the last exn_velocity / exn_generate: inputs uploaded .. result ready to copy back
   cudaEvent_t call_ev[2] = {nullptr, nullptr};
   double last_call_ms = 0;
@@ -535,7 +536,7 @@ void prof_mark(exn_handle* h, int cat) {
 void prof_collect(exn_handle* h) {
   if (!h->prof.on || h->prof.marks.size() < 2) return;
   cudaEventSynchronize(h->prof.marks.back().first);
-  double acc[4] = {0, 0, 0, 0};
+  double acc[5] = {0, 0, 0, 0, 0};
   for (size_t i = 0; i + 1 < h->prof.marks.size(); ++i) {
     float ms = 0;
     cudaEventElapsedTime(&ms, h->prof.marks[i].first, h->prof.marks[i + 1].first);
@@ -543,7 +544,7 @@ void prof_collect(exn_handle* h) {
   }
   for (auto& m : h->prof.marks) cudaEventDestroy(m.first);
   h->prof.marks.clear();
-  for (int i = 0; i < 4; ++i) h->last_ms[i] = acc[i];
+  for (int i = 0; i < 5; ++i) h->last_ms[i] = acc[i];
 }
 
 // ---------------------------------------------------------------------------- one step
@@ -974,7 +975,9 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
   h->launches += 5 + 3 + 7LL * c.layers + 2 + (in.cached ? 0 : (in.ptext > 0 ? 3 : 0) + (in.nref ? 2 : 0));
 
   // timestep
+  prof_mark(h, 2);
   if ((rc = timestep_chain(h, in.sigma))) return rc;
+  prof_mark(h, 0);
   // first pass: this rank's prefix rows [lo, hi) through txt_in (the text rows among them) and
   // img_in (an edit picture's rows among them), straight into its x.  Prefix row of text row t: t
   // before the picture's A rows, t + nref after them; the picture holds prefix rows [a, a + nref).
@@ -1024,7 +1027,9 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
 
   for (int il = 0; il < c.layers; ++il) {
     const size_t kl_off = il * kv_layer;
+    prof_mark(h, 2);
     ln_mod_launch(h->x, h->y, h->modv + 0 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
+    prof_mark(h, 0);
     // QKV: every row's head group g stored by the epilogue straight into rank g's Q and K/V (over
     // NVLink for g != r), at the row's place in the sequence; the all-to-all is the GEMM's stores
     GemmEpi eq;
@@ -1047,7 +1052,9 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     eq.sp_p = P;
     if ((rc = gemm(h, h->y, W, h->w_qkv + static_cast<size_t>(il) * 3 * W * W, W, n_loc, 3 * W, W, EPI_QKV, eq)))
       return rc;
+    prof_mark(h, 4);
     if ((rc = sp_flag_barrier(h))) return rc;
+    prof_mark(h, 1);
     AttnArgs aa;
     aa.q = b.qf;
     aa.k = b.kv + kl_off;
@@ -1074,7 +1081,9 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     aa.sp_nl = Nl;
     aa.sp_img0 = img0;
     if ((rc = attention_launch(aa, h->d_status, h->st))) return fail(h, EXN_ECUDA, "attention launch failed: %d", rc);
+    prof_mark(h, 4);
     if ((rc = sp_flag_barrier(h))) return rc;
+    prof_mark(h, 0);
     GemmEpi eo;
     eo.out = h->x;
     eo.ld_out = W;
@@ -1085,13 +1094,16 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
     eo.p = pl_loc;
     if ((rc = gemm(h, b.att_in, W, h->w_out + static_cast<size_t>(il) * W * W, W, n_loc, W, W, EPI_GATE_RESID, eo)))
       return rc;
+    prof_mark(h, 2);
     ln_mod_launch(h->x, h->y, h->modv + 2 * W, 4 * W, n_loc, W, n_loc, n_loc, 0, 0, pl_loc, 0, h->st);
+    prof_mark(h, 3);
     GemmEpi eg;
     eg.out = h->ff;
     eg.ld_out = c.ffn;
     if ((rc = gemm(h, h->y, W, h->w_gu + static_cast<size_t>(il) * 2 * c.ffn * W, W, n_loc, 2 * c.ffn, W, EPI_SWIGLU,
                    eg)))
       return rc;
+    prof_mark(h, 0);
     GemmEpi ed = eo;
     ed.mod = h->modv + 3 * W;
     if ((rc = gemm(h, h->ff, c.ffn, h->w_down + static_cast<size_t>(il) * W * c.ffn, c.ffn, n_loc, W, c.ffn,
@@ -1099,7 +1111,9 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
       return rc;
   }
   // this rank's image rows: LayerNorm * (1 + sc), proj_out into its latent columns
+  prof_mark(h, 2);
   ln_mod_launch(h->x, h->y, h->sc, 0, Nl, W, Nl, n_loc, pl_loc, 0, 0, 1, h->st);
+  prof_mark(h, 0);
   GemmEpi ep;
   ep.z = in.z ? in.z + size_t(r) * Nl : nullptr;
   ep.vout = in.v ? in.v + size_t(r) * Nl : nullptr;
@@ -1107,6 +1121,7 @@ int run_step_sp(exn_handle* h, const StepIn& in) {
   ep.nimg = Nl;
   ep.zstride = N;
   if ((rc = gemm(h, h->y, W, h->w_proj, W, Nl, c.latent, W, EPI_PROJ, ep))) return rc;
+  prof_mark(h, 2);
   CK(cudaGetLastError());
   return EXN_OK;
 }
@@ -2078,6 +2093,12 @@ int exn_test_wait_probe(exn_handle* h, double seconds) {
 int exn_test_last_call_ms(const exn_handle* h, double* ms) {
   if (!h || !ms) return EXN_EINVAL;
   *ms = h->last_call_ms;
+  return EXN_OK;
+}
+
+int exn_test_last_barrier_ms(exn_handle* h, double* ms) {
+  if (!h || !ms) return fail(h, EXN_EINVAL, "exn_test_last_barrier_ms: null argument");
+  *ms = h->last_ms[4];
   return EXN_OK;
 }
 

@@ -145,6 +145,7 @@ def lib():
                                              ctypes.c_double]),
         "exn_test_weights_digest": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_uint64)]),
         "exn_test_last_profile": (ctypes.c_int, [H] + [ctypes.POINTER(ctypes.c_double)] * 4),
+        "exn_test_last_barrier_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
         "exn_test_profile": (ctypes.c_int, [H, ctypes.c_int]),
         "exn_test_launch_count": (ctypes.c_longlong, [H]),
         "exn_test_last_call_ms": (ctypes.c_int, [H, ctypes.POINTER(ctypes.c_double)]),
@@ -318,7 +319,9 @@ class Dit:
     def last_profile(self):
         g, a, o, u = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
         self._ck(lib().exn_test_last_profile(self.h, ctypes.byref(g), ctypes.byref(a), ctypes.byref(o), ctypes.byref(u)))
-        return dict(gemm_ms=g.value, attn_ms=a.value, other_ms=o.value, gateup_ms=u.value)
+        b = ctypes.c_double()
+        self._ck(lib().exn_test_last_barrier_ms(self.h, ctypes.byref(b)))
+        return dict(gemm_ms=g.value, attn_ms=a.value, other_ms=o.value, gateup_ms=u.value, barrier_ms=b.value)
 
     def launch_count(self):
         return int(lib().exn_test_launch_count(self.h))

@@ -134,6 +134,11 @@ int exn_test_last_call_ms(const exn_handle* h, double* ms);
  * and of the GEMMs the gate_up + SwiGLU ones alone. */
 int exn_test_last_profile(exn_handle* h, double* gemm_ms, double* attn_ms, double* other_ms, double* gateup_ms);
 
+/* With profiling on, the device time of the last call's sequence-parallel barriers (from the end of
+ * the kernel before each barrier to the start of the one after it: the wait for the slowest rank and
+ * for the peers' stores), in ms; 0 on one GPU. */
+int exn_test_last_barrier_ms(exn_handle* h, double* ms);
+
 /* Device time in ms (CUDA events on the decoder's stream) of the last exn_vae_decode, from the
  * latent's upload to the start of the pixels' download. */
 int exn_test_vae_last_ms(const exn_vae* v, double* ms);
