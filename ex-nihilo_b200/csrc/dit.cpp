@@ -1761,6 +1761,47 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
   return check_status(h);
 }
 
+int exn_test_attention_timed(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
+                             int q0, int p, int l, int b0, int b1, int heads, int kv_rows, int reps, double* ms) {
+  if (!h || !q || !k || !v || !out || reps < 1 || !ms) return fail(h, EXN_EINVAL, "exn_test_attention_timed: bad argument");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  AttnArgs aa;
+  aa.q = static_cast<const bf16*>(q);
+  aa.k = static_cast<const bf16*>(k);
+  aa.v = static_cast<const bf16*>(v);
+  aa.out = static_cast<bf16*>(out);
+  aa.batch = batch;
+  aa.nq = nq;
+  aa.q0 = q0;
+  aa.p = p;
+  aa.l = l;
+  aa.b0 = b0;
+  aa.b1 = b1;
+  aa.heads = heads;
+  aa.width = heads * 128;
+  aa.kv_rows = kv_rows;
+  aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+  aa.sms = h->att_sms ? h->att_sms : h->sms;
+  aa.split_mode = h->att_mode;
+  cudaEvent_t ev[2];
+  CK(cudaEventCreate(&ev[0]));
+  CK(cudaEventCreate(&ev[1]));
+  CK(cudaEventRecord(ev[0], h->st));
+  for (int i = 0; i < reps && !rc; ++i)
+    if (attention_launch(aa, h->d_status, h->st)) rc = fail(h, EXN_EINVAL, "attention launch failed");
+  CK(cudaEventRecord(ev[1], h->st));
+  if (!rc) rc = check_status(h);
+  if (!rc) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ev[0], ev[1]);
+    *ms = t / reps;
+  }
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  return rc;
+}
+
 int exn_test_comm_stats(exn_handle* h, long long* settles, long long* sleeps, double* seconds) {
   if (!h) return fail(h, EXN_EINVAL, "exn_test_comm_stats: null handle");
   if (settles) *settles = h->settles;

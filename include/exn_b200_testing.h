@@ -42,6 +42,11 @@ int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, i
 int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                        int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
 
+/* exn_test_attention run REPS times back to back; *MS the mean time of one launch (CUDA events on
+ * the handle's stream, the launches queued without a host wait between them). */
+int exn_test_attention_timed(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
+                             int q0, int p, int l, int b0, int b1, int heads, int kv_rows, int reps, double* ms);
+
 /* Host side of the communicator waits since the handle was opened: how many times the library
  * waited for an NCCL call to be queued (every barrier of a sequence-parallel pass does), how many
  * 50 us sleeps those waits took, and their total wall time in seconds. */

@@ -189,6 +189,27 @@ def test_attention_work_splits_are_bit_identical(dit, nq):
     assert torch.equal(outs[0], outs[2])
 
 
+def test_attention_timed_equals_single_launch(dit):
+    """exn_test_attention_timed queues the same launch REPS times: the output is the single launch's,
+    bit for bit, and the mean time is positive."""
+    import ctypes
+    batch, nq, q0, p, heads = 1, 700, 0, 300, 2
+    w = heads * 128
+    g = torch.Generator().manual_seed(5)
+    q = ((torch.rand(batch, nq, w, generator=g) * 4 - 2)).to(torch.bfloat16).cuda()
+    k = ((torch.rand(batch, nq, w, generator=g) * 4 - 2)).to(torch.bfloat16).cuda()
+    v = ((torch.rand(batch, nq, w, generator=g) * 2 - 1)).to(torch.bfloat16).cuda()
+    o1 = torch.full((batch, nq, w), float("nan"), dtype=torch.bfloat16, device="cuda")
+    o2 = torch.full_like(o1, float("nan"))
+    dit._ck(E.lib().exn_test_attention(dit.h, q.data_ptr(), k.data_ptr(), v.data_ptr(), o1.data_ptr(),
+                                       batch, nq, q0, p, nq, 8, 264, heads, nq))
+    ms = ctypes.c_double(-1.0)
+    dit._ck(E.lib().exn_test_attention_timed(dit.h, q.data_ptr(), k.data_ptr(), v.data_ptr(), o2.data_ptr(),
+                                             batch, nq, q0, p, nq, 8, 264, heads, nq, 5, ctypes.byref(ms)))
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    assert ms.value > 0
+
+
 def test_ln_mod_row_selection(dit):
     # metal-kernels-test.lisp:91-102: rows n0 + t < p take the second modulation row
     wd, n, n0, p = 4096, 9, 3, 6
