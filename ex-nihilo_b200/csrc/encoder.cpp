@@ -41,7 +41,7 @@ constexpr int kMaxTokens = 32768;
 // prompts of at most this many tokens run their GEMMs split along K (their tile grids cover a
 // fraction of the SMs), in at most kMaxSplits parts
 constexpr int kSplitRows = 512;
-constexpr int kMaxSplits = 8;
+constexpr int kMaxSplits = kEncMaxSplits;
 
 struct Spec {
   std::string name;

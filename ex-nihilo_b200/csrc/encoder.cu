@@ -49,7 +49,9 @@ __global__ void k_q8_raw_to_f32(const uint8_t* __restrict__ raw, float* __restri
   out[i] = static_cast<float>(static_cast<int8_t>(blk[2 + (i & 31)])) * __half2float(d);
 }
 
-// ---- the epilogues of a split-K GEMM: PART [splits][n][N] fp32 partials summed in split order
+// ---- the epilogues of a split-K GEMM: PART [splits][n][N] fp32 partials summed in split order.
+// Every part's load is issued before the first sum (the loop bound is the largest split count, the
+// parts beyond SPLITS predicated off), so a thread waits for memory once, not once a part.
 
 // q / k / v: one warp a (row, head of 128 columns); q and k heads RMS-normed (eps 1e-6) times
 // their weight and turned by RoPE on halves (dims j and j + 64 by angle j of ROPE [row][64]);
@@ -66,12 +68,20 @@ __global__ void k_enc_qkv_sum(const float* __restrict__ part, int splits, int n,
   const int N = qw + 2 * kvw;
   const long long stride = static_cast<long long>(n) * N;
   const float* p = part + static_cast<long long>(r) * N + h * 128 + lane;
+  float pv[kEncMaxSplits][4];
+#pragma unroll
+  for (int sp = 0; sp < kEncMaxSplits; ++sp)
+    if (sp < splits)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[sp][i] = p[sp * stride + 32 * i];
   float x[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = p[32 * i];
-  for (int sp = 1; sp < splits; ++sp)
+  for (int i = 0; i < 4; ++i) x[i] = pv[0][i];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] += p[sp * stride + 32 * i];
+  for (int sp = 1; sp < kEncMaxSplits; ++sp)
+    if (sp < splits)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] += pv[sp][i];
   const int col = h * 128;
   const int sec = col < qw ? 0 : (col < qw + kvw ? 1 : 2);
   if (sec < 2) {
@@ -97,60 +107,55 @@ __global__ void k_enc_qkv_sum(const float* __restrict__ part, int splits, int n,
   for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
 }
 
-// one block of 256 threads a row: x [n][w] += the sum of the partials, then (NORM given) xn bf16 =
-// x / sqrt(mean(x^2) + 1e-6) * norm, the next GEMM's operand; w <= 4096, a multiple of 4
-__global__ void __launch_bounds__(256) k_enc_resid_rms(const float* __restrict__ part, int splits, int n, int w,
-                                                       float* __restrict__ x, const float* __restrict__ norm,
-                                                       bf16* __restrict__ xn) {
-  __shared__ float red[8];
-  const int r = blockIdx.x;
+// one block of 1024 threads a row, a float4 of the row a thread: x [n][w] += the sum of the partials,
+// then (NORM given) xn bf16 = x / sqrt(mean(x^2) + 1e-6) * norm, the next GEMM's operand; w <= 4096,
+// a multiple of 4
+__global__ void __launch_bounds__(1024) k_enc_resid_rms(const float* __restrict__ part, int splits, int n, int w,
+                                                        float* __restrict__ x, const float* __restrict__ norm,
+                                                        bf16* __restrict__ xn) {
+  __shared__ float red[32];
+  const int r = blockIdx.x, c = threadIdx.x;
   const int w4 = w / 4;
   const long long stride4 = static_cast<long long>(n) * w4;
-  const float4* p = reinterpret_cast<const float4*>(part) + static_cast<long long>(r) * w4;
-  float4* xr = reinterpret_cast<float4*>(x) + static_cast<long long>(r) * w4;
-  float4 v[4];
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
   float ss = 0.f;
+  if (c < w4) {
+    const float4* p = reinterpret_cast<const float4*>(part) + static_cast<long long>(r) * w4 + c;
+    float4* xr = reinterpret_cast<float4*>(x) + static_cast<long long>(r) * w4 + c;
+    float4 pv[kEncMaxSplits];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = threadIdx.x + 256 * i;
-    if (c < w4) {
-      float4 a = p[c];
-      for (int sp = 1; sp < splits; ++sp) {
-        const float4 b = p[sp * stride4 + c];
-        a.x += b.x;
-        a.y += b.y;
-        a.z += b.z;
-        a.w += b.w;
+    for (int sp = 0; sp < kEncMaxSplits; ++sp)
+      if (sp < splits) pv[sp] = p[sp * stride4];
+    o = *xr;
+    float4 a = pv[0];
+#pragma unroll
+    for (int sp = 1; sp < kEncMaxSplits; ++sp)
+      if (sp < splits) {
+        a.x += pv[sp].x;
+        a.y += pv[sp].y;
+        a.z += pv[sp].z;
+        a.w += pv[sp].w;
       }
-      float4 o = xr[c];
-      o.x += a.x;
-      o.y += a.y;
-      o.z += a.z;
-      o.w += a.w;
-      xr[c] = o;
-      v[i] = o;
-      ss += (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w);
-    }
+    o.x += a.x;
+    o.y += a.y;
+    o.z += a.z;
+    o.w += a.w;
+    *xr = o;
+    ss = (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w);
   }
   if (norm == nullptr) return;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  for (int k = 16; k > 0; k >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, k);
+  if ((c & 31) == 0) red[c >> 5] = ss;
   __syncthreads();
   float t = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) t += red[i];
+  for (int i = 0; i < 32; ++i) t += red[i];
   const float inv = rsqrtf(t / static_cast<float>(w) + 1e-6f);
-  uint2* y = reinterpret_cast<uint2*>(xn + static_cast<long long>(r) * w);
-  const float4* nw = reinterpret_cast<const float4*>(norm);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = threadIdx.x + 256 * i;
-    if (c < w4) {
-      const float4 m = __ldg(nw + c);
-      y[c] = make_uint2(pack_bf16x2(v[i].x * inv * m.x, v[i].y * inv * m.y),
-                        pack_bf16x2(v[i].z * inv * m.z, v[i].w * inv * m.w));
-    }
+  if (c < w4) {
+    const float4 m = __ldg(reinterpret_cast<const float4*>(norm) + c);
+    reinterpret_cast<uint2*>(xn + static_cast<long long>(r) * w)[c] =
+        make_uint2(pack_bf16x2(o.x * inv * m.x, o.y * inv * m.y), pack_bf16x2(o.z * inv * m.z, o.w * inv * m.w));
   }
 }
 
@@ -161,11 +166,20 @@ __global__ void k_enc_swiglu_sum(const float* __restrict__ part, int splits, int
   const int r = static_cast<int>(i / ffn), j = static_cast<int>(i - static_cast<long long>(r) * ffn);
   const long long stride = static_cast<long long>(n) * 2 * ffn;
   const float* p = part + static_cast<long long>(r) * 2 * ffn + (j >> 7) * 256 + (j & 127);
-  float g = p[0], u = p[128];
-  for (int sp = 1; sp < splits; ++sp) {
-    g += p[sp * stride];
-    u += p[sp * stride + 128];
-  }
+  float pg[kEncMaxSplits], pu[kEncMaxSplits];
+#pragma unroll
+  for (int sp = 0; sp < kEncMaxSplits; ++sp)
+    if (sp < splits) {
+      pg[sp] = p[sp * stride];
+      pu[sp] = p[sp * stride + 128];
+    }
+  float g = pg[0], u = pu[0];
+#pragma unroll
+  for (int sp = 1; sp < kEncMaxSplits; ++sp)
+    if (sp < splits) {
+      g += pg[sp];
+      u += pu[sp];
+    }
   h[i] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
 }
 
@@ -197,7 +211,7 @@ void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, c
 
 void enc_resid_rms_launch(const float* part, int splits, int n, int w, float* x, const float* norm, bf16* xn,
                           cudaStream_t st) {
-  k_enc_resid_rms<<<n, 256, 0, st>>>(part, splits, n, w, x, norm, xn);
+  k_enc_resid_rms<<<n, 1024, 0, st>>>(part, splits, n, w, x, norm, xn);
 }
 
 void enc_swiglu_sum_launch(const float* part, int splits, int n, int ffn, bf16* h, cudaStream_t st) {

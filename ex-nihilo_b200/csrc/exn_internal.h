@@ -222,6 +222,8 @@ void enc_rope_launch(const int* pos, float2* table, int n, double theta, cudaStr
 // Q8_0 to f32, exactly: from split (qs, d) or from GGUF's 34-byte blocks
 void q8_to_f32_launch(const int8_t* qs, const __half* d, float* out, long long n, cudaStream_t st);
 void q8_raw_to_f32_launch(const uint8_t* raw, float* out, long long n, cudaStream_t st);
+// the most parts an encoder GEMM is split into along K (the epilogues below take at most this many)
+constexpr int kEncMaxSplits = 8;
 // the epilogues of split-K GEMMs (PART [splits][n][N] fp32, summed in split order): q / k / v with
 // the per-head norms and RoPE on halves; h = silu(gate) * up (interleaved by 128)
 void enc_qkv_sum_launch(const float* part, int splits, int n, int qw, int kvw, const float* norm_q,
