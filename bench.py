@@ -650,29 +650,32 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return None
-    times = []
+    blocks = []
     with all_host_threads():
         threads = cpu_threads()
         for i in range(args.warmup + args.steps):
             bs = cpu_block_seconds()
             if i >= args.warmup:
-                times.append(cpu_picture_seconds(bs))
-    sec = statistics.mean(times)
+                blocks.append(bs)
+    block_s = statistics.mean(blocks)
+    sec = cpu_picture_seconds(block_s)                   # a picture's estimate from the timed blocks
     v = 1.0 / sec
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
-    timed_s = sum(times) / cpu_picture_seconds(1.0)      # the block passes actually run in the timed steps
     return {
         "impl": "reference",
         "metric": METRIC, "value": round(v, 6), "unit": "images/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(block_s * 1e3, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": round(v / PUBLISHED_IMAGES_PER_S, 4), "dtype": "f32", "data": "synthetic",
-        "config": dict(cfg2_config(world, args.batch), parallelism="host CPU (rank 0 alone)"),
+        "config": cfg2_config(world, args.batch),
+        "runs_on": "the host CPU, rank 0 alone (all host threads)",
         "extrapolated": True,
         "timed_unit": "one DiT block",
-        "timed_s": round(timed_s, 2),
-        "extrapolation": "each step times one DiT block at the cached-step size (4096 rows x 4224 keys) and scales "
-                         "it by the %.1f block passes of a picture; ms_per_step is that estimate, not a measured "
-                         "picture" % cpu_picture_seconds(1.0),
+        "timed_s": round(sum(blocks), 2),
+        "ms_per_picture_estimate": round(sec * 1e3, 1),
+        "extrapolation": "each step is a bounded sample of the workload: one DiT block at the cached-step size "
+                         "(4096 rows x 4224 keys), whose time is ms_per_step; value scales it by the %.1f block "
+                         "passes of a picture (ms_per_picture_estimate), not a measured picture"
+                         % cpu_picture_seconds(1.0),
         "cpu_baseline": {"value": round(v, 6), "unit": "images/s", "cores": threads, "kind": "port",
                          "sample": "each step one DiT block at 1024^2 (numpy oracle restating inspect/ref_dit.py; the "
                                    "reference's own ref_dit.py cannot travel to this box), scaled to a picture"},
