@@ -1761,6 +1761,33 @@ int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* 
   return check_status(h);
 }
 
+int exn_test_gemv(exn_handle* h, int kind, const void* w, const void* d, const float* x, float* y, int m, int in,
+                  int out, int act, int piece, int reps, double* ms) {
+  if (!h || !w || !x || !y || (kind == W_Q8 && !d) || kind < W_Q8 || kind > W_F32 || reps < 1 || !ms)
+    return fail(h, EXN_EINVAL, "exn_test_gemv: bad argument");
+  if (m < 1 || m > 2 || in <= 0 || out <= 0 || (act == 2 && piece <= 0))
+    return fail(h, EXN_EINVAL, "exn_test_gemv: bad shape");
+  int rc;
+  if ((rc = use_device(h))) return rc;
+  cudaEvent_t ev[2];
+  CK(cudaEventCreate(&ev[0]));
+  CK(cudaEventCreate(&ev[1]));
+  CK(cudaEventRecord(ev[0], h->st));
+  for (int i = 0; i < reps && !rc; ++i)
+    if (gemv_launch(kind, w, static_cast<const __half*>(d), x, y, m, in, out, act, piece, h->st))
+      rc = fail(h, EXN_EINVAL, "exn_test_gemv: launch failed (shape out of the kernel's range)");
+  CK(cudaEventRecord(ev[1], h->st));
+  if (!rc) rc = check_status(h);
+  if (!rc) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, ev[0], ev[1]);
+    *ms = t / reps;
+  }
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  return rc;
+}
+
 int exn_test_attention_timed(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                              int q0, int p, int l, int b0, int b1, int heads, int kv_rows, int reps, double* ms) {
   if (!h || !q || !k || !v || !out || reps < 1 || !ms) return fail(h, EXN_EINVAL, "exn_test_attention_timed: bad argument");

@@ -130,6 +130,8 @@ def lib():
         "exn_test_gemm_timed": (ctypes.c_int, [H, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.POINTER(ctypes.c_double)]),
         "exn_test_attention": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 9),
+        "exn_test_gemv": (ctypes.c_int, [H, ctypes.c_int, vp, vp, vp, vp] + [ctypes.c_int] * 6 +
+                          [ctypes.POINTER(ctypes.c_double)]),
         "exn_test_attention_timed": (ctypes.c_int, [H, vp, vp, vp, vp] + [ctypes.c_int] * 10 +
                                      [ctypes.POINTER(ctypes.c_double)]),
         "exn_test_gemm_pairs": (ctypes.c_int, [H, ctypes.c_int]),

@@ -42,6 +42,14 @@ int exn_test_gemm_timed(exn_handle* h, const void* a, const void* b, float* c, i
 int exn_test_attention(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,
                        int q0, int p, int l, int b0, int b1, int heads, int kv_rows);
 
+/* The DiT's small-M matrix-vector product (timestep MLP, modulation, norm_out; src/cuda-dit.lisp:157-167)
+ * on device tensors: y [m][out] fp32 = act(x [m][in] fp32 . W^T), m 1 or 2.  KIND 0: W int8 [out][in]
+ * with fp16 scales D [out][in / 32] (Q8_0 split), 1: bf16 [out][in], 2: f32 [out][in].  ACT 0 none,
+ * 1 SiLU, 2 tanh on the second and fourth PIECE-row pieces (the modulation's gates).  Run REPS times
+ * back to back; *MS the mean time of one. */
+int exn_test_gemv(exn_handle* h, int kind, const void* w, const void* d, const float* x, float* y, int m, int in,
+                  int out, int act, int piece, int reps, double* ms);
+
 /* exn_test_attention run REPS times back to back; *MS the mean time of one launch (CUDA events on
  * the handle's stream, the launches queued without a host wait between them). */
 int exn_test_attention_timed(exn_handle* h, const void* q, const void* k, const void* v, void* out, int batch, int nq,

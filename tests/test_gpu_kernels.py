@@ -210,6 +210,63 @@ def test_attention_timed_equals_single_launch(dit):
     assert ms.value > 0
 
 
+# (kind, m, in, out, act, piece): the DiT's four GEMV calls (timestep MLP 256 -> W and W -> W with
+# SiLU, the modulation W -> 4W with tanh on its gate pieces, norm_out) plus bf16 / f32 weights and a
+# row count that is not a multiple of a warp's rows
+GEMV_CASES = [
+    (0, 2, 256, 4096, 1, 0),
+    (0, 2, 4096, 4096, 1, 0),
+    (0, 2, 4096, 16384, 2, 4096),
+    (0, 1, 4096, 4096, 0, 0),
+    (0, 1, 4096, 1000, 0, 0),
+    (1, 2, 4096, 1024, 1, 0),
+    (2, 2, 4096, 1024, 2, 256),
+]
+
+
+@pytest.mark.parametrize("case", GEMV_CASES, ids=["kind%d-m%d-%dx%d-act%d" % c[:5] for c in GEMV_CASES])
+def test_gemv_matches_numpy(dit, case):
+    """k_gemv (the timestep MLP and modulation, src/cuda-dit.lisp:157-167) against a float64 product of
+    the same weights: Q8_0 values q * d exactly as upload-dit keeps them, bf16 or f32 matrices.  The
+    kernel accumulates in fp32 over up to 4096 terms, so the bound is 2e-5 of the output's scale."""
+    import ctypes
+    kind, m, k_in, n_out, act, piece = case
+    rs = np.random.default_rng(k_in + n_out + kind)
+    x = rs.standard_normal((m, k_in)).astype(np.float32)
+    if kind == 0:
+        q = rs.integers(-127, 128, (n_out, k_in)).astype(np.int8)
+        dsc = (rs.uniform(0.5, 1.5, (n_out, k_in // 32)) * 0.02 / 127).astype(np.float16)
+        w = q.astype(np.float64) * np.repeat(dsc.astype(np.float64), 32, axis=1)
+        wd, dd = torch.from_numpy(q).cuda(), torch.from_numpy(dsc).cuda()
+    elif kind == 1:
+        wt = (torch.from_numpy(rs.standard_normal((n_out, k_in)).astype(np.float32)) * 0.02).to(torch.bfloat16)
+        w = wt.double().numpy()
+        wd, dd = wt.cuda(), None
+    else:
+        wf = (rs.standard_normal((n_out, k_in)) * 0.02).astype(np.float32)
+        w = wf.astype(np.float64)
+        wd, dd = torch.from_numpy(wf).cuda(), None
+    want = x.astype(np.float64) @ w.T
+    if act == 1:
+        want = want / (1 + np.exp(-want))
+    elif act == 2:
+        pc = np.arange(n_out) // piece
+        gate = (pc == 1) | (pc == 3)
+        want[:, gate] = np.tanh(want[:, gate])
+    xd = torch.from_numpy(x).cuda()
+    y = torch.full((m, n_out), float("nan"), dtype=torch.float32, device="cuda")
+    ms = ctypes.c_double(-1.0)
+    dit._ck(E.lib().exn_test_gemv(dit.h, kind, wd.data_ptr(), dd.data_ptr() if dd is not None else None,
+                                  xd.data_ptr(), y.data_ptr(), m, k_in, n_out, act, piece, 10, ctypes.byref(ms)))
+    got = y.cpu().numpy().astype(np.float64)
+    err = np.abs(got - want).max() / np.abs(want).max()
+    wbytes = n_out * k_in * (1.0625 if kind == 0 else (2 if kind == 1 else 4))
+    print("\nGEMV kind %d, %d x %d -> %d: max err %.2e of the output's scale; %.1f us a launch, %.2f TB/s of "
+          "weights (10 launches back to back: weights that fit stay in L2)"
+          % (kind, m, k_in, n_out, err, ms.value * 1e3, wbytes / (ms.value * 1e-3) / 1e12))
+    assert np.isfinite(got).all() and err < 2e-5
+
+
 def test_ln_mod_row_selection(dit):
     # metal-kernels-test.lisp:91-102: rows n0 + t < p take the second modulation row
     wd, n, n0, p = 4096, 9, 3, 6
